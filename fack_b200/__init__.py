@@ -1,0 +1,31 @@
+"""fack_b200 -- B200 (sm_100a) FP8 block-scaled GEMM.
+
+Drop-in for the one data-parallel path of feifei14119/FACK: aiter's
+``gemm_a8w8_blockscale_bpreshuffle`` operator.  The arithmetic is a
+hand-written tcgen05/TMA kernel behind a C ABI (include/fack_gemm.h); this
+package is the PyTorch-facing operator surface and the N-sharded multi-GPU
+wrapper.
+"""
+from .ops import (  # noqa: F401
+    AITER_SYMBOLS,
+    device_status,
+    gather_interleave,
+    gemm_a8w8_blockscale_bpreshuffle,
+    gemm_a8w8_blockscale_bpreshuffle_asm,
+    gemm_blockscale,
+    get_config,
+    shuffle_weight,
+    workspace_size,
+)
+
+__all__ = [
+    "AITER_SYMBOLS",
+    "device_status",
+    "gather_interleave",
+    "gemm_a8w8_blockscale_bpreshuffle",
+    "gemm_a8w8_blockscale_bpreshuffle_asm",
+    "gemm_blockscale",
+    "get_config",
+    "shuffle_weight",
+    "workspace_size",
+]

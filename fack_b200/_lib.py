@@ -1,0 +1,87 @@
+"""ctypes binding of the C-ABI library ``libfack_gemm.so`` (include/fack_gemm.h).
+
+Loading fails loudly: there is no CPU or library fallback for the GEMM, so a
+missing or stale build raises instead of silently computing something else.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libfack_gemm.so"
+
+# Status codes, mirrored from enum fack_status.
+FACK_OK = 0
+FACK_ERR_BAD_SHAPE = 1
+FACK_ERR_BAD_ALIGN = 2
+FACK_ERR_BAD_STRIDE = 3
+FACK_ERR_WS_TOO_SMALL = 4
+FACK_ERR_LAUNCH = 5
+FACK_ERR_UNSUPPORTED_ARCH = 6
+FACK_ERR_BAD_ARG = 7
+FACK_ERR_DEVICE_TIMEOUT = 8
+FACK_ERR_CUDA = 9
+
+FACK_W_ROW_MAJOR = 0
+FACK_W_PACKED = 1
+
+# Every symbol the header declares, with its ctypes signature.
+_c_int, _c_i64, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t
+SIGNATURES = {
+    "fack_status_string": (ctypes.c_char_p, [_c_int]),
+    "fack_version": (_c_int, []),
+    "fack_gemm_bs_select": (_c_int, [_c_int, _c_int, _c_int, _c_int,
+                                     ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "fack_gemm_bs_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_sz)]),
+    "fack_gemm_bs_prepack_w": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p]),
+    "fack_gemm_bs": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
+                              _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
+    "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
+    "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
+}
+
+_lib = None
+
+
+def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
+    """Load (once) and type the C-ABI library; raises if it is missing."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(
+            f"{p} is not built; run `python -m fack_b200.build` (nvcc, sm_100a). "
+            "The FP8 block-scaled GEMM has no fallback implementation.")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def status_string(code: int) -> str:
+    return load().fack_status_string(int(code)).decode()
+
+
+class FackError(RuntimeError):
+    """Raised for a non-zero status from the C ABI."""
+
+    def __init__(self, code: int, what: str):
+        self.code = int(code)
+        super().__init__(f"{what}: {status_string(code)} (status {code})")
+
+
+def check(code: int, what: str) -> None:
+    if code == FACK_OK:
+        return
+    if code in (FACK_ERR_BAD_SHAPE, FACK_ERR_BAD_STRIDE, FACK_ERR_BAD_ARG, FACK_ERR_BAD_ALIGN):
+        # contract violations are ValueError before any launch, as in the
+        # reference driver (client/aiter/hsa/gfx942/driver.py:11-12)
+        raise ValueError(f"{what}: {status_string(code)} (status {code})")
+    raise FackError(code, what)

@@ -1,0 +1,62 @@
+"""Build recipe for the in-tree C-ABI library ``fack_b200/libfack_gemm.so``.
+
+The library is compiled straight with nvcc for sm_100a only (B200); there is
+no torch extension and no JIT cache, so the built ``.so`` sits beside this
+file and travels with the source tree.  ``python -m fack_b200.build`` builds it;
+``build(verbose=True)`` prints ptxas register / spill / shared-memory usage.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+CSRC = HERE / "csrc"
+LIB = HERE / "libfack_gemm.so"
+SOURCES = [CSRC / "gemm_bs_sm100.cu"]
+HEADERS = [CSRC / "sm100_ptx.cuh", ROOT / "include" / "fack_gemm.h"]
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found; the FP8 GEMM library needs CUDA 12.8+ for sm_100a")
+    return cand
+
+
+def needs_build() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the library if any source is newer than it (or ``force``)."""
+    if not force and not needs_build():
+        return LIB
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [
+        nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+        "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr",
+        "-I", str(ROOT / "include"),
+        *(["-Xptxas", "-v"] if verbose else []),
+        *map(str, SOURCES), "-o", str(tmp),
+    ]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
+    if verbose:
+        sys.stdout.write(res.stdout + res.stderr)
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(LIB)

@@ -1,0 +1,275 @@
+"""PyTorch operator surface of the B200 FP8 block-scaled GEMM.
+
+Two layers:
+
+* the aiter-compatible entry points a user of the reference calls, with the
+  same names, argument order and meaning:
+
+  - ``gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale,
+    bias=None, splitK=None, kernelName=None, bpreshuffle=True,
+    zero_bias_buf=None)`` -- the low-level operator the reference times
+    (client/aiter/hsa/gfx942/driver.py:26-29; signature observed at
+    client/aiter/hsa/gfx942/dispatch_driver.py:62-63);
+  - ``gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale,
+    dtype=torch.bfloat16)`` -- the public entry that picks the kernel and
+    split-K itself and allocates ``out``
+    (client/aiter/hsa/gfx942/dispatch_driver.py:72-74);
+  - ``shuffle_weight(b, layout=(16, 16))`` -- the weight pre-pack step
+    (client/aiter/hsa/gfx942/driver.py:21), here producing this library's own
+    tile-blocked, pre-swizzled layout;
+  - ``get_config(M, N, K)`` -- the tuned-config lookup stand-in
+    (client/aiter/dispatch.py:23-35), returning this library's choice.
+
+  As in aiter, ``x_scale`` for these entry points carries the reference's
+  transposed-contiguous bytes: a contiguous ``(M, K/128)`` view whose storage
+  is ``K/128``-major (``sa.T.contiguous().view_as(sa)``,
+  client/aiter/hsa/gfx942/driver.py:22).  A non-contiguous ``(M, K/128)``
+  view with strides ``(1, M)`` (the same bytes) is accepted too.
+
+* ``gemm_blockscale(xq, wq, x_scale, w_scale, out=None, split_k=0)`` -- the
+  native entry, which reads ``x_scale`` through its logical strides, so a
+  plain row-major ``[M, K/128]`` tensor works as is.
+
+Every entry validates on the host and raises ``ValueError`` for a contract
+violation before launching, like the reference driver
+(client/aiter/hsa/gfx942/driver.py:11-12).  Calls allocate nothing except the
+split-K workspace, which is cached per (device, stream) and grown only outside
+CUDA-graph capture, so a warmed-up call is capturable.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+FP8 = torch.float8_e4m3fn
+BLOCK = 128
+
+# gfx942 tile symbols the reference reviews (client/aiter/hsa/gfx942/optest_driver.py:20-24).
+# They name AMD code objects; on B200 they are accepted and map to this
+# library's own tile choice.
+AITER_SYMBOLS = frozenset(
+    "_ZN5aiter{}fp8gemm_bf16_blockscale_BpreShuffle_{}x128E".format(43 if t == 128 else 42, t)
+    for t in (32, 48, 64, 80, 96, 128))
+KERNEL_PREFIX = "fack_bs_sm100"
+
+_workspaces: dict = {}
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def kernel_name(tile_m: int, split_k: int) -> str:
+    return f"{KERNEL_PREFIX}_t{tile_m}x128_s{split_k}"
+
+
+def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
+    """Kernel and split-K this library uses for (M, N, K) on the current device."""
+    lib = _lib.load()
+    tm, sk = ctypes.c_int(), ctypes.c_int()
+    _lib.check(lib.fack_gemm_bs_select(int(M), int(N), int(K), int(split_k), ctypes.byref(tm),
+                                       ctypes.byref(sk)), "fack_gemm_bs_select")
+    return {"libtype": "asm", "kernelName": kernel_name(tm.value, sk.value), "splitK": sk.value,
+            "tile_m": tm.value, "tile_n": BLOCK}
+
+
+def workspace_size(M: int, N: int, K: int, split_k: int = 0) -> int:
+    lib = _lib.load()
+    nb = ctypes.c_size_t()
+    _lib.check(lib.fack_gemm_bs_workspace_size(int(M), int(N), int(K), int(split_k), ctypes.byref(nb)),
+               "fack_gemm_bs_workspace_size")
+    return nb.value
+
+
+def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
+    if nbytes == 0:
+        return None
+    key = (device.index, _stream_handle(device))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                "split-K workspace must grow during CUDA-graph capture; call the operator once "
+                "with this shape before capturing")
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _check_common(xq, wq, w_scale, out, M, N, K):
+    for name, t in (("XQ", xq), ("WQ", wq), ("w_scale", w_scale), ("out", out)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+    if xq.dtype != FP8 or wq.dtype != FP8:
+        raise ValueError("XQ and WQ must be torch.float8_e4m3fn")
+    if w_scale.dtype != torch.float32 or out.dtype != torch.bfloat16:
+        raise ValueError("w_scale must be float32 and out bfloat16")
+    if M < 1 or N % BLOCK or K % BLOCK or N <= 0 or K <= 0:
+        raise ValueError("blockscale GEMM requires positive M and N%128 == K%128 == 0")
+    if tuple(wq.shape) != (N, K) or tuple(out.shape) != (M, N):
+        raise ValueError(f"shape mismatch: XQ {tuple(xq.shape)}, WQ {tuple(wq.shape)}, out {tuple(out.shape)}")
+    if tuple(w_scale.shape) != (N // BLOCK, K // BLOCK) or not w_scale.is_contiguous():
+        raise ValueError(f"w_scale must be a contiguous [{N // BLOCK}, {K // BLOCK}] float32 tensor")
+    if xq.stride(1) != 1 or wq.stride(1) != 1 or not wq.is_contiguous() or out.stride(1) != 1:
+        raise ValueError("XQ, WQ and out must be K-contiguous / row-contiguous")
+    devs = {t.device for t in (xq, wq, w_scale, out)}
+    if len(devs) != 1:
+        raise ValueError("all tensors must be on one device")
+
+
+def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k):
+    M, K = xq.shape
+    N = wq.shape[0]
+    dev = xq.device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        need = workspace_size(M, N, K, split_k)
+        ws = _workspace(dev, need)
+        st = lib.fack_gemm_bs(
+            xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
+            x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0),
+            M, N, K, int(split_k), _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
+    _lib.check(st, "fack_gemm_bs")
+    return out
+
+
+def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
+                    out: Optional[torch.Tensor] = None, split_k: int = 0) -> torch.Tensor:
+    """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
+
+    ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
+    :func:`shuffle_weight` (detected by its ``is_shuffled`` mark).
+    """
+    if xq.dim() != 2 or wq.dim() != 2:
+        raise ValueError("XQ and WQ must be 2-D")
+    M, K = xq.shape
+    N = wq.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
+    _check_common(xq, wq, w_scale, out, M, N, K)
+    if x_scale.dtype != torch.float32 or not x_scale.is_cuda or tuple(x_scale.shape) != (M, K // BLOCK):
+        raise ValueError(f"x_scale must be a float32 CUDA tensor of shape [{M}, {K // BLOCK}]")
+    sm, sk = x_scale.stride()
+    if K // BLOCK == 1:
+        sk = max(sk, 1)
+    if M == 1:
+        sm = max(sm, 1)
+    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k)
+
+
+def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):
+    """(stride_m, stride_kb) of the reference's transposed-contiguous x_scale."""
+    if x_scale.dtype != torch.float32 or not x_scale.is_cuda or tuple(x_scale.shape) != (M, KB):
+        raise ValueError(f"x_scale must be a float32 CUDA tensor of shape [{M}, {KB}]")
+    if x_scale.is_contiguous() or x_scale.stride() == (1, M):
+        # bytes are K/128-major with M contiguous, whatever the view's strides say
+        return 1, M
+    raise ValueError("x_scale must be the transposed-contiguous view sa.T.contiguous().view_as(sa)")
+
+
+def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None, splitK=None, kernelName=None,
+                                         bpreshuffle=True, zero_bias_buf=None):
+    """Drop-in for aiter's ``gemm_a8w8_blockscale_bpreshuffle_asm`` (writes and returns ``out``).
+
+    ``bias`` must be None: the blockscale operator has no bias term
+    (client/aiter/hsa/gfx942/dispatch_driver.py:66-67); ``zero_bias_buf`` is
+    accepted and unused.  ``kernelName`` may be None, one of the reviewed
+    gfx942 symbols or one of this library's names; ``splitK`` None/0 lets the
+    library choose.  ``bpreshuffle=True`` requires ``b`` from
+    :func:`shuffle_weight`.
+    """
+    if bias is not None:
+        raise ValueError("the blockscale operator takes no bias")
+    if kernelName not in (None, "") and kernelName not in AITER_SYMBOLS and not str(kernelName).startswith(
+            KERNEL_PREFIX):
+        raise ValueError(f"unknown blockscale kernel {kernelName!r}")
+    shuffled = bool(getattr(b, "is_shuffled", False))
+    if bool(bpreshuffle) != shuffled:
+        raise ValueError("bpreshuffle={} but the weight {} a shuffle_weight() output".format(
+            bool(bpreshuffle), "is" if shuffled else "is not"))
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("a and b must be 2-D")
+    M, K = a.shape
+    N = b.shape[0]
+    _check_common(a, b, w_scale, out, M, N, K)
+    sm, sk = _aiter_xscale_strides(x_scale, M, K // BLOCK)
+    split = 0 if splitK is None else int(splitK)
+    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split)
+
+
+def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bfloat16):
+    """Drop-in for aiter's public ``gemm_a8w8_blockscale_bpreshuffle``: selects
+    the kernel and split-K for (M, N, K), allocates ``out`` and calls the
+    low-level operator once (the behaviour pinned by
+    unittests/test_aiter_dispatch.py:452-505)."""
+    if dtype != torch.bfloat16:
+        raise ValueError("only bfloat16 output is supported")
+    M, K = x.shape
+    N = weight.shape[0]
+    cfg = get_config(M, N, K)
+    out = torch.empty((M, N), dtype=dtype, device=x.device)
+    return gemm_a8w8_blockscale_bpreshuffle_asm(x, weight, out, x_scale, w_scale, None, cfg["splitK"],
+                                                cfg["kernelName"], bool(getattr(weight, "is_shuffled", False)))
+
+
+def shuffle_weight(b: torch.Tensor, layout=(16, 16)) -> torch.Tensor:
+    """Pre-pack an e4m3 ``[N, K]`` weight into this library's tile layout.
+
+    Stand-in for aiter's ``shuffle_weight(b, layout=(16, 16))``
+    (client/aiter/hsa/gfx942/driver.py:21).  The returned tensor has the same
+    shape and dtype, holds 128x128 tiles in their 128-byte-swizzled shared
+    memory image, and is marked ``is_shuffled = True``.  ``layout`` is
+    accepted for signature compatibility; the only supported value is
+    ``(16, 16)``.
+    """
+    if tuple(layout) != (16, 16):
+        raise ValueError("only layout=(16, 16) is supported")
+    if not isinstance(b, torch.Tensor) or not b.is_cuda or b.dtype != FP8 or b.dim() != 2:
+        raise ValueError("shuffle_weight needs a 2-D float8_e4m3fn CUDA tensor")
+    N, K = b.shape
+    if N % BLOCK or K % BLOCK:
+        raise ValueError("shuffle_weight requires N%128 == K%128 == 0")
+    if b.stride(1) != 1:
+        raise ValueError("weight rows must be contiguous")
+    packed = torch.empty((N, K), dtype=FP8, device=b.device)
+    lib = _lib.load()
+    with torch.cuda.device(b.device):
+        st = lib.fack_gemm_bs_prepack_w(b.data_ptr(), b.stride(0), None, N, K, packed.data_ptr(), None,
+                                        _stream_handle(b.device))
+    _lib.check(st, "fack_gemm_bs_prepack_w")
+    packed.is_shuffled = True
+    return packed
+
+
+def gather_interleave(gathered: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[m, r*ns + c] = gathered[r, m, c] on the GPU (N-sharded output assembly)."""
+    if gathered.dim() != 3 or out.dim() != 2 or gathered.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise ValueError("gathered must be bf16 [g, M, n_shard] and out bf16 [M, g*n_shard]")
+    g, M, ns = gathered.shape
+    if tuple(out.shape) != (M, g * ns) or not gathered.is_contiguous() or out.stride(1) != 1:
+        raise ValueError("gather_interleave shape/layout mismatch")
+    lib = _lib.load()
+    with torch.cuda.device(out.device):
+        st = lib.fack_gather_interleave(gathered.data_ptr(), g, M, ns, out.data_ptr(), out.stride(0),
+                                        _stream_handle(out.device))
+    _lib.check(st, "fack_gather_interleave")
+    return out
+
+
+def device_status(reset: bool = False) -> int:
+    """Error flags set by kernels whose bounded waits expired (0 = none); synchronises."""
+    lib = _lib.load()
+    flags = ctypes.c_uint()
+    st = lib.fack_device_status(_stream_handle(torch.device("cuda", torch.cuda.current_device())),
+                                ctypes.byref(flags), 1 if reset else 0)
+    if st not in (_lib.FACK_OK, _lib.FACK_ERR_DEVICE_TIMEOUT):
+        _lib.check(st, "fack_device_status")
+    return flags.value

@@ -1,0 +1,147 @@
+/*
+ * fack_gemm.h -- C ABI of the B200 (sm_100a) FP8 block-scaled GEMM library.
+ *
+ * Computes, for e4m3 activations XQ[M,K] and weights WQ[N,K] (both K-major),
+ *
+ *   Y[m,n] (bf16) = sum_kb ( sum_{k in block kb} XQ[m,k] * WQ[n,k] )
+ *                        * x_scale[m,kb] * w_scale[n/128,kb]
+ *
+ * with one fp32 activation scale per token per 128-wide K block and one fp32
+ * weight scale per 128x128 weight block.  This is the arithmetic of the
+ * reference's fp32 oracle, client/aiter/hsa/gfx942/driver.py:18-20, and of the
+ * aiter operator it times, gemm_a8w8_blockscale_bpreshuffle_asm
+ * (client/aiter/hsa/gfx942/driver.py:26-29; signature observed at
+ * client/aiter/hsa/gfx942/dispatch_driver.py:62-63).
+ *
+ * Contract shared by every entry point:
+ *   - plain pointers and sizes only; `stream` is a cudaStream_t (NULL = legacy
+ *     default stream) passed as void*;
+ *   - every argument is validated on the host and a non-zero status is
+ *     returned before anything is launched; nothing aborts the process;
+ *   - no entry point allocates, frees or synchronises, so every launch can be
+ *     captured in a CUDA graph (the caller sizes and owns the workspace);
+ *   - the device must be sm_100 (B200); other devices return
+ *     FACK_ERR_UNSUPPORTED_ARCH.
+ */
+#ifndef FACK_GEMM_H
+#define FACK_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fack_status {
+  FACK_OK = 0,
+  FACK_ERR_BAD_SHAPE = 1,       /* M<1, N or K not a positive multiple of 128 */
+  FACK_ERR_BAD_ALIGN = 2,       /* a pointer is NULL or misaligned */
+  FACK_ERR_BAD_STRIDE = 3,      /* leading dimension / scale stride invalid */
+  FACK_ERR_WS_TOO_SMALL = 4,    /* split-K workspace missing or too small */
+  FACK_ERR_LAUNCH = 5,          /* the CUDA launch itself failed */
+  FACK_ERR_UNSUPPORTED_ARCH = 6,/* current device is not sm_100 */
+  FACK_ERR_BAD_ARG = 7,         /* other invalid argument (split_k, layout, g) */
+  FACK_ERR_DEVICE_TIMEOUT = 8,  /* a kernel gave up waiting (device status) */
+  FACK_ERR_CUDA = 9             /* a CUDA runtime query failed */
+};
+
+/* Weight layouts accepted by fack_gemm_bs (argument `wq_packed`). */
+enum fack_w_layout {
+  FACK_W_ROW_MAJOR = 0,  /* WQ[N,K], row stride K bytes                       */
+  FACK_W_PACKED = 1      /* output of fack_gemm_bs_prepack_w                   */
+};
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* fack_status_string(int status);
+
+/* Library ABI version: 100 * major + minor. */
+int fack_version(void);
+
+/*
+ * Tile / split-K plan the library uses for an (M,N,K) problem on the current
+ * device.  split_k_request = 0 asks for the library's own choice (the stand-in
+ * for aiter's tuned-CSV lookup get_CKGEMM_config, see
+ * client/aiter/dispatch.py:23-35 and unittests/test_aiter_dispatch.py:472-477);
+ * a positive value is validated and echoed.  tile_m receives the token tile
+ * (UMMA N extent), split_k the number of K slices.
+ */
+int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
+                        int* tile_m, int* split_k);
+
+/*
+ * Bytes of workspace fack_gemm_bs needs for this problem and split (0 when the
+ * plan has a single K slice).  Replaces the allocation the aiter launcher does
+ * internally (csrc/py_itfs_cu/asm_a8w8_blockscale_bpreshuffle.cu, a missing
+ * upstream file named at client/aiter/hsa/gfx942/manifest.json:12).
+ */
+int fack_gemm_bs_workspace_size(int M, int N, int K, int split_k, size_t* bytes);
+
+/*
+ * Optional weight pre-pack, the stand-in for aiter's BpreShuffle
+ * (shuffle_weight(b, layout=(16,16)), client/aiter/hsa/gfx942/driver.py:21).
+ * Rewrites WQ[N,K] (row stride ldw bytes) into 128x128 tiles, tile (nb,kb) at
+ * ((nb*K/128)+kb)*16384 bytes, each tile stored in the exact 128-byte-swizzled
+ * image the kernel's shared-memory stage expects, so one TMA box per tile is a
+ * straight 16 KB copy.  wq_packed must hold N*K bytes.  w_scale needs no
+ * repacking: ws_packed may be NULL; when it is not, the [N/128,K/128] fp32
+ * scales are copied there unchanged.
+ */
+int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale,
+                           int N, int K, void* wq_packed, float* ws_packed,
+                           void* stream);
+
+/*
+ * The GEMM.  Replaces aiter's gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out,
+ * x_scale, w_scale, bias=None, splitK, kernelName, bpreshuffle, zero_bias_buf)
+ * (client/aiter/hsa/gfx942/dispatch_driver.py:62-63; positional launch tuple
+ * pinned at unittests/test_aiter_dispatch.py:504-505).
+ *
+ *   xq        e4m3 activations, row m at xq + m*ldx (ldx >= K, ldx % 16 == 0)
+ *   wq        e4m3 weights, FACK_W_ROW_MAJOR ([N,K], row stride K) or
+ *             FACK_W_PACKED (fack_gemm_bs_prepack_w output)
+ *   x_scale   fp32, element (m,kb) at x_scale[m*xs_stride_m + kb*xs_stride_kb];
+ *             the reference's transposed-contiguous view
+ *             (sa.T.contiguous().view_as(sa), driver.py:22) is
+ *             xs_stride_m = 1, xs_stride_kb = M; logical row-major is
+ *             xs_stride_m = K/128, xs_stride_kb = 1
+ *   w_scale   fp32 [N/128, K/128] row-major
+ *   out       bf16 [M,N], row stride ldo elements (ldo >= N, ldo % 8 == 0);
+ *             every element of the MxN block is written exactly once
+ *   split_k   0 = library choice, else 1..8 (and <= K/128)
+ *   workspace fp32 partials for split_k > 1, at least
+ *             fack_gemm_bs_workspace_size() bytes, 16-byte aligned
+ *
+ * The split-K reduction is deterministic: slices are summed in a fixed order,
+ * so repeated calls give bitwise-identical outputs.
+ */
+int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed,
+                 const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,
+                 const float* w_scale, void* out, int64_t ldo,
+                 int M, int N, int K, int split_k,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Column interleave for the N-sharded multi-GPU path: `gathered` holds g
+ * contiguous bf16 shards [g][M][n_shard] (the layout an all-gather of each
+ * rank's [M, n_shard] output produces); writes out[m, r*n_shard + c] =
+ * gathered[r][m][c] with row stride ldo.  n_shard % 8 == 0, ldo % 8 == 0.
+ * No reference counterpart: the reference runs one GPU per process
+ * (client/aiter/docs/validation.md:42-46).
+ */
+int fack_gather_interleave(const void* gathered, int g, int M, int n_shard,
+                           void* out, int64_t ldo, void* stream);
+
+/*
+ * Reads (and with reset != 0 clears) the current device's error word, which a
+ * kernel sets when a bounded wait inside it gives up.  Synchronises `stream`.
+ * *flags == 0 means no kernel has reported a problem.  Returns
+ * FACK_ERR_DEVICE_TIMEOUT when flags are set, FACK_OK otherwise.
+ */
+int fack_device_status(void* stream, unsigned int* flags, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FACK_GEMM_H */

@@ -1,0 +1,58 @@
+"""CPU: the aiter-compatible Python entry points refuse bad calls on the host
+(ValueError before any launch), as the reference driver does."""
+import pytest
+import torch
+
+import fack_b200 as fb
+from fack_b200 import ops
+
+FP8 = torch.float8_e4m3fn
+
+
+def cpu_case(M=32, N=256, K=512):
+    a = torch.zeros(M, K, dtype=FP8)
+    b = torch.zeros(N, K, dtype=FP8)
+    out = torch.empty(M, N, dtype=torch.bfloat16)
+    xs = torch.ones(M, K // 128)
+    ws = torch.ones(N // 128, K // 128)
+    return a, b, out, xs, ws
+
+
+def test_bias_is_rejected():
+    a, b, out, xs, ws = cpu_case()
+    with pytest.raises(ValueError, match="bias"):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, xs, ws, bias=torch.zeros(1, 256))
+
+
+def test_unknown_kernel_rejected_and_aiter_symbols_accepted_by_name():
+    a, b, out, xs, ws = cpu_case()
+    with pytest.raises(ValueError, match="unknown blockscale kernel"):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, xs, ws, kernelName="no_such_kernel")
+    assert len(fb.AITER_SYMBOLS) == 6
+    assert "_ZN5aiter43fp8gemm_bf16_blockscale_BpreShuffle_128x128E" in fb.AITER_SYMBOLS
+
+
+def test_bpreshuffle_flag_must_match_weight():
+    a, b, out, xs, ws = cpu_case()
+    with pytest.raises(ValueError, match="bpreshuffle"):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, xs, ws, bpreshuffle=True)
+
+
+def test_cpu_tensors_rejected_no_fallback():
+    a, b, out, xs, ws = cpu_case()
+    with pytest.raises(ValueError, match="CUDA"):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, xs, ws, bpreshuffle=False)
+    with pytest.raises(ValueError, match="CUDA"):
+        fb.gemm_blockscale(a, b, xs, ws, out=out)
+    with pytest.raises(ValueError):
+        fb.shuffle_weight(b)
+
+
+def test_public_entry_rejects_non_bf16_output():
+    a, b, out, xs, ws = cpu_case()
+    with pytest.raises(ValueError, match="bfloat16"):
+        fb.gemm_a8w8_blockscale_bpreshuffle(a, b, xs, ws, dtype=torch.float16)
+
+
+def test_kernel_names_are_stable():
+    assert ops.kernel_name(256, 6) == "fack_bs_sm100_t256x128_s6"
