@@ -1,0 +1,484 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 FP8 block-scaled GEMM (one JSON line on rank 0).
+
+Metric: FP8 blockscale GEMM TFLOPS (2*M*N*K per call), with HBM GB/s and the
+roofline fraction of the GEMM kernel, and us/call.
+
+Default workload: the single-GPU decode shape M=256, N=3072, K=7168 (fp32
+block scales, e4m3 operands, bf16 output), called exactly as the reference's
+timed run does -- pre-packed weight, transposed-contiguous x_scale,
+``gemm_a8w8_blockscale_bpreshuffle_asm(a, packed_b, out, packed_sa, sb, ...)``
+(client/aiter/hsa/gfx942/driver.py:26-29).  A step is one call on one input
+set; steps rotate over enough distinct input sets that the rotation exceeds
+2.5x the 126 MB L2, and are timed as CUDA-graph replays with CUDA events
+(client/aiter/runner.py:160-189 times graph replays the same way).
+
+``--gpus N`` under torchrun: the decode / plumbing / sweep workloads do not
+shard, so N ranks run N independent replicas (weak scaling, no collective).
+``--workload prefill|wide_constant|wide_uniform`` shards the output columns
+over the ranks and all-gathers the bf16 output over NCCL every step (strong
+scaling).
+
+``--impl reference`` times the reference's own algorithm for this path -- the
+fp32 dequantise-then-matmul of client/aiter/hsa/gfx942/driver.py:18-20 -- on
+the host cores (the oracle port; the reference's GPU path needs gfx942 and the
+absent aiter submodule), on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "FP8 blockscale GEMM TFLOPS & HBM GB/s (% roofline), us/call"
+SHARDED = ("prefill", "wide_constant", "wide_uniform")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks --
+class ClockSampler:
+    """NVML sampler (SM clock, max clock, clock-event reasons) for one GPU."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.samples = []
+        self.ok = False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report no clocks rather than guess
+            self.err = str(e)
+
+    def _sample(self):
+        nv = self.nv
+        try:
+            reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        self.samples.append((time.time(), nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), int(reasons)))
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": getattr(self, "err", "no samples")}
+        mask = 0
+        for _, _, r in self.samples:
+            mask |= r
+        reasons = [name for bit, name in self.REASONS.items() if mask & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(s[1] for s in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- workloads --
+def env_ranks():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def make_sets(wl, n_sets, dev, shard):
+    """n_sets distinct device copies of (a, packed_b, out, packed_sa, sb)."""
+    from fack_b200 import data
+    import fack_b200 as fb
+    xq, xs = data.make_activations(wl.M, wl.K, wl.x_dist, seed=0, device=dev)
+    wq, ws = data.make_weights(wl.N, wl.K, wl.w_dist, seed=1, device=dev)
+    if shard is not None:
+        from fack_b200.dist import shard_weight
+        wq, ws = shard_weight(wq, ws, *shard)
+    packed = fb.shuffle_weight(wq)
+    del wq
+    sa = data.to_aiter_xscale(xs)
+    sets = []
+    for i in range(n_sets):
+        cp = (lambda t: t.clone()) if i else (lambda t: t)
+        b = cp(packed)
+        b.is_shuffled = True
+        sets.append({"a": cp(xq), "b": b, "sa": cp(sa), "sa_logical": cp(xs), "sb": cp(ws),
+                     "out": torch.empty((wl.M, packed.shape[0]), dtype=torch.bfloat16, device=dev)})
+    return sets
+
+
+def capture(fn_steps, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn_steps()
+    return g
+
+
+def timed_graph_replay(graphs, stream):
+    """Replay [(graph, times)], bracketed by CUDA events on `stream`; ms."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        start.record(stream)
+        for g, times in graphs:
+            for _ in range(times):
+                g.replay()
+        end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def load_traffic(workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload, {}).get("bytes_per_launch")
+    except Exception:
+        return None
+
+
+def cpu_oracle_rate(wl, budget_s: float, max_steps: int = 3):
+    """Time the CPU oracle on a bounded column sample of `wl`; TFLOPS and sample text."""
+    from fack_b200 import data
+    from oracle.blockscale import reference_gemm
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    xq, xs = data.make_activations(wl.M, wl.K, wl.x_dist, seed=0)
+    n_cols = 128
+    wq, ws = data.make_weights(n_cols, wl.K, "normal", seed=1)
+    t0 = time.perf_counter()
+    reference_gemm(xq, wq, xs, ws)
+    t1 = time.perf_counter() - t0
+    # grow the column sample to fill ~budget/steps per call, up to the full N
+    per_call = budget_s / max_steps
+    n_cols = int(min(wl.N, max(128, 128 * math.floor(per_call / max(t1, 1e-4)))))
+    n_cols -= n_cols % 128
+    wq, ws = data.make_weights(n_cols, wl.K, "normal", seed=1)
+    times = []
+    for _ in range(max_steps):
+        t0 = time.perf_counter()
+        reference_gemm(xq, wq, xs, ws)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    tflops = data.flops(wl.M, n_cols, wl.K) / t / 1e12
+    sample = (f"M={wl.M} x N={n_cols} (of {wl.N}) x K={wl.K} of workload {wl.name}: dequantise both operands + "
+              f"fp32 matmul + bf16 round (driver.py:18-20), median of {max_steps} calls, {t * 1e3:.1f} ms/call")
+    return tflops, threads, sample
+
+
+# ------------------------------------------------------------- our arm --
+def run_ours(args):
+    import fack_b200 as fb
+    from fack_b200 import data
+    rank, world, local = env_ranks()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    wl = data.WORKLOADS[args.workload]
+    sharded = args.workload in SHARDED and world > 1
+    shard = (rank, world) if sharded else None
+    n_local = wl.N // world if sharded else wl.N
+    set_bytes = data.algorithmic_bytes(wl.M, n_local, wl.K)
+    n_sets = args.rotate or max(1, math.ceil(2.5 * L2_BYTES / set_bytes))
+    sets = make_sets(wl, n_sets, dev, shard)
+    cfg = fb.get_config(wl.M, n_local, wl.K)
+    stream = torch.cuda.Stream(dev)
+
+    sharder = None
+    if sharded:
+        from fack_b200.dist import ShardedBlockscaleGemm
+        sharder = ShardedBlockscaleGemm()
+        full_out = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(n_sets)]
+
+    def gemm_call(s):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(s["a"], s["b"], s["out"], s["sa"], s["sb"], None,
+                                                cfg["splitK"], cfg["kernelName"], True)
+
+    def step(i):
+        s = sets[i % n_sets]
+        if sharded:
+            sharder(s["a"], s["b"], s["sa_logical"], s["sb"], out=full_out[i % n_sets])
+        else:
+            gemm_call(s)
+
+    # warm-up (eager: sizes the split-K workspace and the gather buffer)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    barrier(world)
+
+    chunk = max(n_sets, (min(args.steps, 1024) // n_sets) * n_sets)
+    full, rem = divmod(args.steps, chunk)
+    with torch.cuda.stream(stream):
+        g_chunk = capture(lambda: [step(i) for i in range(chunk)], stream) if full else None
+        g_rem = capture(lambda: [step(i) for i in range(rem)], stream) if rem else None
+        g_gemm = None
+        if sharded:  # GEMM-only graph for the kernel roofline
+            g_gemm = capture(lambda: [gemm_call(sets[i % n_sets]) for i in range(chunk)], stream)
+    plan = [(g_chunk, full)] if full else []
+    if rem:
+        plan.append((g_rem, 1))
+
+    # keep the GPU busy ~0.3 s before timing so clocks are sampled under load
+    sampler = ClockSampler(local)
+    sampler.start()
+    probe = g_chunk or g_rem
+    t_probe = timed_graph_replay([(probe, 1)], stream) / 1e3
+    timed_graph_replay([(probe, max(1, int(0.3 / max(t_probe, 1e-6))))], stream)
+    barrier(world)
+    ms = timed_graph_replay(plan, stream)
+    sampler.stop()
+    barrier(world)
+    ms = max_over_ranks(ms, world, dev)
+
+    us_call = ms * 1e3 / args.steps
+    ranks_work = world if not sharded else 1
+    total_flops = data.flops(wl.M, wl.N, wl.K) * ranks_work * args.steps
+    value = total_flops / (ms / 1e3) / 1e12
+
+    # roofline of the GEMM kernel (per launch on one GPU)
+    if sharded:
+        k_ms = timed_graph_replay([(g_gemm, 1)], stream)
+        k_us = max_over_ranks(k_ms * 1e3 / chunk, world, dev)
+    else:
+        k_us = us_call
+    peaks = measured_peaks()
+    k_bytes = data.algorithmic_bytes(wl.M, n_local, wl.K)
+    k_flops = data.flops(wl.M, n_local, wl.K)
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    t_mem = k_bytes / (peaks["hbm_gbs"] * 1e3)        # us
+    t_tc = k_flops / (fp8_peak * 1e6)                 # us
+    hbm_gbs = k_bytes / (k_us * 1e3)
+    tflops_k = k_flops / (k_us * 1e6)
+    if t_mem >= t_tc:
+        roof = {"bound": "hbm", "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(hbm_gbs / peaks["hbm_gbs"], 4)}
+    else:
+        roof = {"bound": "tensor", "achieved": round(tflops_k, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                "frac": round(tflops_k / fp8_peak, 4)}
+    roof.update({"traffic": load_traffic(args.workload), "algorithmic_bytes": k_bytes,
+                 "kernel_us": round(k_us, 3), "peak_source": (
+                     f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 burst "
+                     f"{peaks['bf16_tflops']} TFLOP/s"),
+                 "t_mem_us": round(t_mem, 3), "t_tc_us": round(t_tc, 3),
+                 "frac_of_max_roof": round(max(t_mem, t_tc) / k_us, 4)})
+
+    # e2e through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, wl, sets[0], dev, stream, sharder, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tfl, cores, sample = cpu_oracle_rate(wl, budget_s=args.cpu_budget)
+        cpu = {"value": round(tfl, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample}
+
+    clocks = sampler.summary()
+    per_step_launches = 2 if sharded else 1  # GEMM (+ column interleave when sharded)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 6), "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate, bf16 out)",
+        "data": "synthetic (seeded; benchmark-config construction, scale = amax/240)",
+        "config": {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "M": wl.M, "N": wl.N, "K": wl.K,
+                   "x_dist": wl.x_dist, "w_dist": wl.w_dist, "tile_m": cfg["tile_m"], "split_k": cfg["splitK"],
+                   "kernel": cfg["kernelName"], "weights": "prepacked (bpreshuffle=True)",
+                   "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB = {n_sets * set_bytes / 1e6:.0f} MB"
+                         f" (> 126 MB L2)",
+                   "timing": "CUDA-graph replay, CUDA events on the launch stream, max over ranks",
+                   "parallelism": (f"N-shard g={world} + NCCL all-gather" if sharded else
+                                   ("single GPU" if world == 1 else f"{world} independent replicas"))},
+        "us_per_call": round(us_call, 3), "hbm_gbs": round(data.algorithmic_bytes(wl.M, n_local, wl.K) /
+                                                           (k_us * 1e3), 1),
+        "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "gpu_launches": per_step_launches * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    status = fb.device_status()
+    if status:
+        log(f"device status flags set: {status:#x}")
+    del g_chunk, g_rem, g_gemm, plan, probe
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    if status:
+        sys.exit(3)
+
+
+def run_e2e(args, wl, s0, dev, stream, sharder, world):
+    """Public API, host inputs: per step H2D of XQ + x_scale (pinned), the call, D2H of Y."""
+    import fack_b200 as fb
+    steps = min(args.steps, args.e2e_steps)
+    a_h = s0["a"].cpu().pin_memory()
+    sa_h = (s0["sa_logical"] if sharder else s0["sa"]).cpu().pin_memory()
+    n_out = wl.N
+    y_h = torch.empty((wl.M, n_out), dtype=torch.bfloat16).pin_memory()
+    a_d = torch.empty_like(s0["a"])
+    sa_d = torch.empty_like(s0["sa"])
+    full = torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) if sharder else None
+
+    def one():
+        a_d.copy_(a_h, non_blocking=True)
+        sa_d.copy_(sa_h, non_blocking=True)
+        if sharder:
+            y = sharder(a_d, s0["b"], sa_d, s0["sb"], out=full)
+        else:
+            y = fb.gemm_a8w8_blockscale_bpreshuffle(a_d, s0["b"], sa_d, s0["sb"], dtype=torch.bfloat16)
+        y_h.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            one()
+        end.record(stream)
+        end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world, dev)
+    from fack_b200 import data
+    work = data.flops(wl.M, wl.N, wl.K) * (1 if sharder else world) * steps
+    return {"value": round(work / (ms / 1e3) / 1e12, 4), "unit": "TFLOPS",
+            "h2d_bytes_per_step": a_h.numel() * a_h.element_size() + sa_h.numel() * 4,
+            "d2h_bytes_per_step": y_h.numel() * 2, "steps": steps, "us_per_step": round(ms * 1e3 / steps, 2),
+            "api": "fack_b200.gemm_a8w8_blockscale_bpreshuffle (public entry, allocates out, selects kernel)"}
+
+
+# ------------------------------------------------------- reference arm --
+def run_reference(args):
+    rank, world, _ = env_ranks()
+    if rank != 0:
+        return
+    from fack_b200 import data
+    from oracle.blockscale import reference_gemm
+    wl = data.WORKLOADS[args.workload]
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    xq, xs = data.make_activations(wl.M, wl.K, wl.x_dist, seed=0)
+    # size the per-step column sample so warm-up + steps fit the time budget
+    wq, ws = data.make_weights(128, wl.K, "normal" if wl.w_dist == "normal" else wl.w_dist, seed=1)
+    t0 = time.perf_counter()
+    reference_gemm(xq, wq, xs, ws)
+    t128 = time.perf_counter() - t0
+    per_step = args.ref_budget / max(1, args.steps + args.warmup)
+    n_cols = int(min(wl.N, max(128, 128 * math.floor(per_step / max(t128, 1e-5)))))
+    n_cols -= n_cols % 128
+    wq, ws = data.make_weights(n_cols, wl.K, "normal" if wl.w_dist == "normal" else wl.w_dist, seed=1)
+    for _ in range(args.warmup):
+        reference_gemm(xq, wq, xs, ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_gemm(xq, wq, xs, ws)
+    dt = time.perf_counter() - t0
+    value = data.flops(wl.M, n_cols, wl.K) * args.steps / dt / 1e12
+    sample = (f"M={wl.M} x N={n_cols} (of {wl.N}) x K={wl.K} per step of workload {wl.name}: fp32 dequantise + "
+              f"matmul + bf16 (client/aiter/hsa/gfx942/driver.py:18-20 restated), torch CPU, {threads} threads")
+    line = {"metric": METRIC, "value": round(value, 5), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantised e4m3)",
+            "data": "synthetic (seeded; benchmark-config construction)", "impl": "reference",
+            "config": {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "M": wl.M, "N": wl.N, "K": wl.K,
+                       "parallelism": "host CPU, rank 0 only"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "TFLOPS", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="decode")
+    ap.add_argument("--rotate", type=int, default=0, help="input sets to rotate (0 = enough to exceed L2)")
+    ap.add_argument("--e2e-steps", type=int, default=500)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle work for cpu_baseline")
+    ap.add_argument("--ref-budget", type=float, default=90.0, help="seconds for the reference arm's steps")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.steps < 1:
+        ap.error("--steps must be >= 1")
+    from fack_b200 import data
+    if args.workload not in data.WORKLOADS:
+        ap.error(f"unknown workload; choose from {sorted(data.WORKLOADS)}")
+    _, world, _ = env_ranks()
+    if world != args.gpus:
+        ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

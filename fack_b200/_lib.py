@@ -35,6 +35,10 @@ SIGNATURES = {
     "fack_gemm_bs_select": (_c_int, [_c_int, _c_int, _c_int, _c_int,
                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "fack_gemm_bs_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_sz)]),
+    "fack_gemm_bs_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int),
+                                   ctypes.POINTER(_c_int), ctypes.POINTER(_c_sz)]),
+    "fack_gemm_bs_ex": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
+                                 _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
     "fack_gemm_bs_prepack_w": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p]),
     "fack_gemm_bs": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                               _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),

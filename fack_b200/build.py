@@ -8,6 +8,7 @@ file and travels with the source tree.  ``python -m fack_b200.build`` builds it;
 from __future__ import annotations
 
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -44,8 +45,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     cmd = [
         nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
         "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr",
-        "-I", str(ROOT / "include"),
-        *(["-Xptxas", "-v"] if verbose else []),
+        "-I", str(ROOT / "include"), "-Xptxas", "-v",
         *map(str, SOURCES), "-o", str(tmp),
     ]
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -53,8 +53,34 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
     if verbose:
         sys.stdout.write(res.stdout + res.stderr)
+    check_ptxas(res.stdout + res.stderr)
     os.replace(tmp, LIB)
     return LIB
+
+
+GEMM_LAUNCH_REGS = 168  # the kernel's setmaxnreg split is sized for this count
+
+
+def check_ptxas(log: str) -> None:
+    """Every GEMM kernel variant must use exactly GEMM_LAUNCH_REGS registers and
+    spill nothing (the host refuses to launch it otherwise)."""
+    entry, found = None, 0
+    for line in log.splitlines():
+        m = re.search(r"Compiling entry function '(\S+)'", line)
+        if m:
+            entry = m.group(1)
+            continue
+        if entry and "gemm_bs_kernel" in entry:
+            m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+            if m and (int(m.group(1)) or int(m.group(2))):
+                raise RuntimeError(f"{entry} spills registers: {line.strip()}")
+            m = re.search(r"Used (\d+) registers", line)
+            if m:
+                found += 1
+                if int(m.group(1)) != GEMM_LAUNCH_REGS:
+                    raise RuntimeError(f"{entry} uses {m.group(1)} registers, expected {GEMM_LAUNCH_REGS}")
+    if found == 0:
+        raise RuntimeError("ptxas report lists no GEMM kernel")
 
 
 if __name__ == "__main__":

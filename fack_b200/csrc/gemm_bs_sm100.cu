@@ -6,23 +6,29 @@
 // reference's fp32 oracle for aiter's gemm_a8w8_blockscale_bpreshuffle_asm).
 //
 // Design (B200-first, not a translation of the gfx942 kernels):
-//  * swap-AB: the 128 weight rows of a tile are the UMMA M side (TMEM lanes),
-//    the tokens are the UMMA N side (TMEM columns, 32..256).  A 128-row weight
-//    tile lies inside one 128x128 scale block, so w_scale is one scalar per
-//    (tile, kb) and x_scale is one value per TMEM column.
-//  * per 128-wide K block (kb): TMA brings a 128x128 B weight tile and a
-//    BNx128 B token tile into a multi-stage mbarrier ring (128-byte swizzle);
-//    one thread issues 4 tcgen05.mma (K=32 each) into one of two TMEM
-//    buffers; 8 epilogue warps read the finished buffer with tcgen05.ld and
-//    fold it into fp32 register accumulators with acc += partial *
-//    (x_scale * w_scale) -- the per-block rescale cannot go into the MMA
-//    because the scales are arbitrary fp32 values, not UE8M0 powers of two.
-//    The double-buffered TMEM lets the MMA of kb+1 overlap the rescale of kb.
+//  * a CTA owns a 128-token x BN-weight-row output tile (BN = 64/128/256):
+//    the tokens are the UMMA M side (TMEM lanes), the weight rows the UMMA N
+//    side (TMEM columns).  Each thread of the rescale warps owns one token,
+//    so the per-K-block scale it needs is one scalar,
+//    x_scale[m,kb] * w_scale[n/128,kb] (two for a 256-row tile, one per half).
+//  * per 128-wide K block (kb): TMA brings the 128x128 B token tile and the
+//    BNx128 B weight tile into a multi-stage mbarrier ring (128-byte
+//    swizzle); one thread issues 4 tcgen05.mma (K=32 each) into one of 2-4
+//    TMEM buffers; 8 rescale warps (two per TMEM lane quarter) read the
+//    finished buffer with tcgen05.ld and fold it into fp32 register
+//    accumulators, acc += partial * scale -- the per-block rescale cannot go
+//    into the MMA because the scales are arbitrary fp32 values, not UE8M0
+//    powers of two.  Several TMEM buffers let the MMA run ahead of the
+//    rescale.  Warpgroup 0 (TMA, MMA) gives registers to the two rescale
+//    warpgroups with setmaxnreg.  Scales are prefetched a few K blocks ahead
+//    with cp.async into per-thread shared slots.
 //  * split-K for small M: the K slices of one output tile form a thread-block
 //    cluster along grid z.  Each CTA writes its fp32 partial tile to the
 //    workspace, the cluster barrier publishes them, and each CTA then sums a
 //    disjoint set of rows over all slices in slice order 0..S-1, so results
 //    are bitwise reproducible and no CTA ever spins on another.
+//  * outputs (bf16 tile or fp32 partial) are staged in shared memory with a
+//    padded pitch and written with coalesced 16-byte stores.
 //  * every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
 //    CTA raises an abort flag, records a code in the device status word,
 //    drains its in-flight TMA copies and MMAs, frees TMEM and exits.
@@ -43,13 +49,22 @@
 namespace fack {
 
 constexpr int kBlk = 128;          // quantisation block along K and N
-constexpr int kTileW = 128;        // weight rows per CTA (UMMA M)
-constexpr int kThreads = 384;      // 12 warps
-constexpr int kEpiWarp0 = 4;       // warps 4..11 rescale and store
+constexpr int kTileM = 128;        // tokens per CTA (UMMA M, TMEM lanes)
+constexpr int kThreads = 384;      // 12 warps = 3 warpgroups
+constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..11 rescale and store
 constexpr int kEpiWarps = 8;
-constexpr int kScaleRing = 4;      // depth of the combined-scale ring
+constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
 constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kSmemBudget = 196608;
+// Register split (setmaxnreg).  The kernel is launched with kLaunchRegs per
+// thread (ptxas' cap for 384 threads, 3 warps per scheduler); warpgroup 0
+// gives registers back and warpgroups 1-2 take them.  Per scheduler: one
+// control warp + two rescale warps = kCtrlRegs + 2 * kEpiRegs <= 3 * kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kCtrlRegs = 64;
+constexpr int kEpiRegs = 216;
+static_assert(kCtrlRegs + 2 * kEpiRegs <= 3 * kLaunchRegs, "register split exceeds the launch allocation");
+static_assert(kCtrlRegs % 8 == 0 && kEpiRegs % 8 == 0, "setmaxnreg counts are multiples of 8");
 
 // Device status word: set by kernels whose bounded waits expired.
 __device__ unsigned int g_status;
@@ -57,32 +72,34 @@ __device__ unsigned int g_status;
 enum : unsigned int {
   kStProducer = 1u,
   kStMma = 2u,
-  kStScale = 4u,
   kStEpilogue = 8u,
   kStDrain = 16u
 };
 
 template <int BN>
 struct Cfg {
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "token tile must be 32..256, multiple of 32");
-  static constexpr int kABytes = kTileW * kBlk;            // 16 KB weight tile
-  static constexpr int kBBytes = BN * kBlk;                 // token tile
+  static_assert(BN == 64 || BN == 128 || BN == 256, "weight tile must be 64, 128 or 256 rows");
+  static constexpr int kABytes = kTileM * kBlk;             // 16 KB token tile
+  static constexpr int kBBytes = BN * kBlk;                 // weight tile
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
-  static constexpr int kTmemBuf = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  static constexpr int kTmemCols = 2 * kTmemBuf;            // power of two, >= 64
-  static constexpr int kCpw = BN / 2;                       // columns per epilogue warp
+  static constexpr int kTmemBufs = (512 / BN) > 4 ? 4 : (512 / BN);
+  static constexpr int kTmemCols = kTmemBufs * BN;          // 512, 512, 256: powers of two
+  static constexpr int kCpw = BN / 2;                       // columns per rescale warp
+  static constexpr int kPitch32 = BN + 4;                   // fp32 staging pitch (floats)
+  static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
   // shared-memory carve-up (offsets from a 1024-byte aligned base)
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kStages * kABytes;
-  static constexpr int kOffScale = kOffB + kStages * kBBytes;
-  static constexpr int kOffBar = kOffScale + kScaleRing * BN * 4;
-  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kScaleRing + 1;
+  static constexpr int kOffRaw = kOffB + kStages * kBBytes;                 // prefetched x_scale [kPrefetch][256]
+  static constexpr int kOffRawW = kOffRaw + kPrefetch * 256 * 4;            // prefetched w_scale [kPrefetch][256]
+  static constexpr int kOffBar = kOffRawW + kPrefetch * 256 * 4;
+  static constexpr int kNumBars = 2 * kStages + 2 * kTmemBufs + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
   static_assert(kStages >= 2, "pipeline needs two stages");
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
-  static_assert(kStages * kABytes >= BN * kTileW * 2, "output staging must fit in the A ring");
+  static_assert(kTileM * kPitch32 * 4 <= kOffRaw, "fp32 output staging must fit in the stage ring");
 };
 
 struct Params {
@@ -91,7 +108,7 @@ struct Params {
   const float* w_scale;        // [N/128][K/128]
   __nv_bfloat16* out;
   int64_t ldo;
-  float* partials;             // [tiles][S][BN][128] fp32, S > 1 only
+  float* partials;             // [tiles][S][128][BN] fp32, S > 1 only
   int M, N, K, KB;
   int split;
   int w_packed;
@@ -111,25 +128,25 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int nt = blockIdx.x;                 // weight tile (128 output columns)
-  const int mt = blockIdx.y;                 // token tile
+  const int nt = blockIdx.x;                 // weight tile (BN output columns)
+  const int mt = blockIdx.y;                 // token tile (128 output rows)
   const int s = blockIdx.z;                  // K slice
   const int S = p.split;
-  const int m0 = mt * BN;
-  const int n0 = nt * kTileW;
+  const int m0 = mt * kTileM;
+  const int n0 = nt * BN;
   const int kb0 = (s * p.KB) / S;
   const int kb1 = ((s + 1) * p.KB) / S;
   const int nk = kb1 - kb0;
+  const int rows = min(kTileM, p.M - m0);    // valid tokens in this tile (>= 1)
+  const int quarters = (rows + 31) >> 5;     // TMEM lane quarters holding valid tokens
+  const int active_warps = 2 * quarters;     // rescale warps with work
 
-  float* csc = reinterpret_cast<float*>(smem + C::kOffScale);
   const uint32_t bar0 = base + C::kOffBar;
   auto bar_full = [&](int i) { return bar0 + 8u * i; };
   auto bar_empty = [&](int i) { return bar0 + 8u * (C::kStages + i); };
   auto bar_tfull = [&](int i) { return bar0 + 8u * (2 * C::kStages + i); };
-  auto bar_tempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + 2 + i); };
-  auto bar_sfull = [&](int i) { return bar0 + 8u * (2 * C::kStages + 4 + i); };
-  auto bar_sempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + 4 + kScaleRing + i); };
-  const uint32_t bar_drain = bar0 + 8u * (2 * C::kStages + 4 + 2 * kScaleRing);
+  auto bar_tempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + C::kTmemBufs + i); };
+  const uint32_t bar_drain = bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
@@ -138,13 +155,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(bar_full(i), 1);
       mbar_init(bar_empty(i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::kTmemBufs; ++i) {
       mbar_init(bar_tfull(i), 1);
-      mbar_init(bar_tempty(i), kEpiWarps);
-    }
-    for (int i = 0; i < kScaleRing; ++i) {
-      mbar_init(bar_sfull(i), 32);
-      mbar_init(bar_sempty(i), kEpiWarps);
+      mbar_init(bar_tempty(i), active_warps);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -167,136 +180,162 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
   int produced = 0;  // TMA stages issued (producer lane only)
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer --
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();   // weights stream once
-      const uint64_t pol_x = policy_evict_last();    // tokens are re-read by every weight tile
-      for (int i = 0; i < nk; ++i) {
-        const int st = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        if (!wait_bounded(bar_empty(st), ph ^ 1u, abort_flag, status, kStProducer, tmo)) break;
-        const int kb = kb0 + i;
-        mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
-        const uint32_t sa = base + C::kOffA + st * C::kABytes;
-        const uint32_t sb = base + C::kOffB + st * C::kBBytes;
-        if (p.w_packed)
-          tma_load_2d(sa, &tmap_w, bar_full(st), 0, (nt * p.KB + kb) * kBlk, pol_w);
-        else
-          tma_load_2d(sa, &tmap_w, bar_full(st), kb * kBlk, n0, pol_w);
-        tma_load_2d(sb, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
-        produced = i + 1;
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer --
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(kTileW, BN);
-      for (int i = 0; i < nk; ++i) {
-        const int st = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        const int buf = i & 1;
-        const uint32_t bph = (i >> 1) & 1;
-        if (!wait_bounded(bar_tempty(buf), bph ^ 1u, abort_flag, status, kStMma, tmo)) break;
-        if (!wait_bounded(bar_full(st), ph, abort_flag, status, kStMma, tmo)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + buf * C::kTmemBuf;
-        const uint64_t da = sw128_kmajor_desc(base + C::kOffA + st * C::kABytes);
-        const uint64_t db = sw128_kmajor_desc(base + C::kOffB + st * C::kBBytes);
-#pragma unroll
-        for (int k = 0; k < kBlk / 32; ++k)  // K = 32 e4m3 elements = 32 bytes = 2 descriptor units
-          umma_f8(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
-        umma_commit(bar_empty(st));
-        umma_commit(bar_tfull(buf));
-      }
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------ combined-scale ring --
-    const float* wsc = p.w_scale + static_cast<int64_t>(nt) * p.KB;
-    for (int i = 0; i < nk; ++i) {
-      const int r = i % kScaleRing;
-      const uint32_t ph = (i / kScaleRing) & 1;
-      if (!wait_bounded(bar_sempty(r), ph ^ 1u, abort_flag, status, kStScale, tmo)) break;
-      const int kb = kb0 + i;
-      const float sw = __ldg(wsc + kb);
-      float* dst = csc + r * BN;
-      for (int j = lane; j < BN; j += 32) {
-        const int m = m0 + j;
-        dst[j] = (m < p.M) ? __ldg(p.x_scale + m * p.xs_sm + kb * p.xs_sk) * sw : 0.0f;
-      }
-      mbar_arrive(bar_sfull(r));
-    }
-  }
-
-  // ------------------------------------------------------------ epilogue --
-  float acc[C::kCpw];
-  const bool is_epi = warp >= kEpiWarp0;
-  const int q = warp & 3;                       // TMEM lane quarter this warp may access
-  const int h = (warp - kEpiWarp0) >> 2;        // column half
-  const int col0 = h * C::kCpw;
-  if (is_epi) {
-#pragma unroll
-    for (int j = 0; j < C::kCpw; ++j) acc[j] = 0.0f;
-    for (int i = 0; i < nk; ++i) {
-      const int buf = i & 1;
-      const uint32_t bph = (i >> 1) & 1;
-      const int r = i % kScaleRing;
-      const uint32_t sph = (i / kScaleRing) & 1;
-      // tcgen05.ld is .sync.aligned: the whole warp must agree before using it.
-      bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
-      got = got && wait_bounded(bar_sfull(r), sph, abort_flag, status, kStEpilogue, tmo);
-      if (!__all_sync(0xffffffffu, got)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * C::kTmemBuf + col0;
-      const float4* sc = reinterpret_cast<const float4*>(csc + r * BN + col0);
-#pragma unroll
-      for (int c = 0; c + 32 <= C::kCpw; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c, v);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float4 f = sc[(c >> 2) + t];
-          acc[c + 4 * t + 0] = fmaf(__uint_as_float(v[4 * t + 0]), f.x, acc[c + 4 * t + 0]);
-          acc[c + 4 * t + 1] = fmaf(__uint_as_float(v[4 * t + 1]), f.y, acc[c + 4 * t + 1]);
-          acc[c + 4 * t + 2] = fmaf(__uint_as_float(v[4 * t + 2]), f.z, acc[c + 4 * t + 2]);
-          acc[c + 4 * t + 3] = fmaf(__uint_as_float(v[4 * t + 3]), f.w, acc[c + 4 * t + 3]);
-        }
-      }
-      if constexpr (C::kCpw % 32 == 16) {
-        constexpr int c = C::kCpw - 16;
-        uint32_t v[16];
-        tmem_ld16(taddr + c, v);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float4 f = sc[(c >> 2) + t];
-          acc[c + 4 * t + 0] = fmaf(__uint_as_float(v[4 * t + 0]), f.x, acc[c + 4 * t + 0]);
-          acc[c + 4 * t + 1] = fmaf(__uint_as_float(v[4 * t + 1]), f.y, acc[c + 4 * t + 1]);
-          acc[c + 4 * t + 2] = fmaf(__uint_as_float(v[4 * t + 2]), f.z, acc[c + 4 * t + 2]);
-          acc[c + 4 * t + 3] = fmaf(__uint_as_float(v[4 * t + 3]), f.w, acc[c + 4 * t + 3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
+  if (warp < kEpiWarp0) {
+    // Control warpgroup: hand registers to the two rescale warpgroups.
+    regs_dec<kCtrlRegs>();
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer --
       if (lane == 0) {
-        mbar_arrive(bar_tempty(buf));
-        mbar_arrive(bar_sempty(r));
+        const uint64_t pol_w = policy_evict_first();   // weights stream once
+        const uint64_t pol_x = policy_evict_last();    // tokens are re-read by every weight tile
+        for (int i = 0; i < nk; ++i) {
+          const int st = i % C::kStages;
+          const uint32_t ph = (i / C::kStages) & 1;
+          if (!wait_bounded(bar_empty(st), ph ^ 1u, abort_flag, status, kStProducer, tmo)) break;
+          const int kb = kb0 + i;
+          mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+          const uint32_t sa = base + C::kOffA + st * C::kABytes;
+          const uint32_t sb = base + C::kOffB + st * C::kBBytes;
+          tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
+          if (p.w_packed) {
+            // packed: tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128
+#pragma unroll
+            for (int t = 0; t < (BN + 127) / 128; ++t) {
+              const int nb = (n0 >> 7) + t;
+              tma_load_2d(sb + t * 16384, &tmap_w, bar_full(st), 0, (nb * p.KB + kb) * kBlk + (n0 & 127), pol_w);
+            }
+          } else {
+            tma_load_2d(sb, &tmap_w, bar_full(st), kb * kBlk, n0, pol_w);
+          }
+          produced = i + 1;
+        }
+      }
+    } else if (warp == 1) {
+      // -------------------------------------------------------- MMA issuer --
+      if (lane == 0) {
+        constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, BN);
+        for (int i = 0; i < nk; ++i) {
+          const int st = i % C::kStages;
+          const uint32_t ph = (i / C::kStages) & 1;
+          const int buf = i % C::kTmemBufs;
+          const uint32_t bph = (i / C::kTmemBufs) & 1;
+          if (!wait_bounded(bar_tempty(buf), bph ^ 1u, abort_flag, status, kStMma, tmo)) break;
+          if (!wait_bounded(bar_full(st), ph, abort_flag, status, kStMma, tmo)) break;
+          tc_fence_after();
+          const uint32_t d = tmem_base + buf * BN;
+          const uint64_t da = sw128_kmajor_desc(base + C::kOffA + st * C::kABytes);
+          const uint64_t db = sw128_kmajor_desc(base + C::kOffB + st * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBlk / 32; ++k)  // K = 32 e4m3 elements = 32 bytes = 2 descriptor units
+            umma_f8(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+          umma_commit(bar_empty(st));
+          umma_commit(bar_tfull(buf));
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------- rescale / epilogue --
+    regs_inc<kEpiRegs>();
+    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int h = (warp - kEpiWarp0) >> 2;        // column half
+    const int col0 = h * C::kCpw;
+    const int tok = q * 32 + lane;                // token row inside the tile
+    if (q < quarters) {
+      float acc[C::kCpw];
+#pragma unroll
+      for (int j = 0; j < C::kCpw; ++j) acc[j] = 0.0f;
+      // Scales: x_scale[m0+tok, kb] and w_scale[block of this column half, kb]
+      // prefetched kPrefetch K blocks ahead with cp.async into this thread's
+      // private shared slots (one commit group per K block).
+      const int et = (warp - kEpiWarp0) * 32 + lane;
+      const bool has = tok < rows;
+      const float* xs_row = p.x_scale + static_cast<int64_t>(has ? m0 + tok : m0) * p.xs_sm;
+      const float* ws_row = p.w_scale + static_cast<int64_t>((n0 + col0) >> 7) * p.KB;
+      const uint32_t raw_x = base + C::kOffRaw + et * 4;
+      const uint32_t raw_w = base + C::kOffRawW + et * 4;
+      const float* raw_xp = reinterpret_cast<const float*>(smem + C::kOffRaw) + et;
+      const float* raw_wp = reinterpret_cast<const float*>(smem + C::kOffRawW) + et;
+      auto prefetch = [&](int i) {  // copies for K block kb0 + i into slot i % kPrefetch
+        if (i < nk) {
+          const int off = (i % kPrefetch) * 256 * 4;
+          const int kb = kb0 + i;
+          cp_async4(raw_x + off, xs_row + static_cast<int64_t>(kb) * p.xs_sk, has ? 4u : 0u);
+          cp_async4(raw_w + off, ws_row + kb, 4u);
+        }
+        cp_async_commit();  // one group per K block, empty past the end
+      };
+#pragma unroll
+      for (int d = 0; d < kPrefetch; ++d) prefetch(d);
+      bool done = true;
+      for (int i = 0; i < nk; ++i) {
+        const int buf = i % C::kTmemBufs;
+        const uint32_t bph = (i / C::kTmemBufs) & 1;
+        cp_async_wait<kPrefetch - 1>();  // this thread's copies for K block i have landed
+        const float sc = raw_xp[(i % kPrefetch) * 256] * raw_wp[(i % kPrefetch) * 256];
+        prefetch(i + kPrefetch);
+        // tcgen05.ld is .sync.aligned: the whole warp must agree before using it.
+        const bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
+        if (!__all_sync(0xffffffffu, got)) {
+          done = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + col0;
+        // Double-buffered 32-column TMEM loads: chunk c+1 is in flight while
+        // chunk c is folded into the accumulators.
+        constexpr int kChunks = C::kCpw / 32;
+        uint32_t va[32], vb[32];
+        tmem_ld32_nowait(taddr, va);
+        tmem_wait32(va);
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          if ((c & 1) == 0) {
+            if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, vb);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) acc[c * 32 + t] = fmaf(__uint_as_float(va[t]), sc, acc[c * 32 + t]);
+            if (c + 1 < kChunks) tmem_wait32(vb);
+          } else {
+            if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, va);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) acc[c * 32 + t] = fmaf(__uint_as_float(vb[t]), sc, acc[c * 32 + t]);
+            if (c + 1 < kChunks) tmem_wait32(va);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty(buf));
+      }
+      cp_async_wait<0>();  // no copy may land after the CTA exits
+      if (done && *abort_flag == 0) {
+        // Stage this thread's row segment in the idle stage ring (every TMA
+        // copy was consumed and the last MMA reading it completed before this
+        // warp's final wait); the padded pitch spreads rows over banks.
+        if (S > 1) {
+          float* row = reinterpret_cast<float*>(smem + C::kOffA) + tok * C::kPitch32 + col0;
+#pragma unroll
+          for (int j = 0; j < C::kCpw; j += 4)
+            *reinterpret_cast<float4*>(row + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        } else {
+          __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffA) + tok * C::kPitch16 + col0;
+#pragma unroll
+          for (int j = 0; j < C::kCpw; j += 8) {
+            uint4 v;
+            __nv_bfloat162 b0 = __floats2bfloat162_rn(acc[j + 0], acc[j + 1]);
+            __nv_bfloat162 b1 = __floats2bfloat162_rn(acc[j + 2], acc[j + 3]);
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[j + 4], acc[j + 5]);
+            __nv_bfloat162 b3 = __floats2bfloat162_rn(acc[j + 6], acc[j + 7]);
+            v.x = *reinterpret_cast<uint32_t*>(&b0);
+            v.y = *reinterpret_cast<uint32_t*>(&b1);
+            v.z = *reinterpret_cast<uint32_t*>(&b2);
+            v.w = *reinterpret_cast<uint32_t*>(&b3);
+            *reinterpret_cast<uint4*>(row + j) = v;
+          }
+        }
       }
     }
   }
 
   // ------------------------------------------------------------ teardown --
-  const int n_loc = q * 32 + lane;  // epilogue thread's weight row inside the tile
-  if (is_epi && S > 1 && *abort_flag == 0) {
-    // fp32 partial tile, rows = tokens, 128 floats per row (coalesced 128 B per warp store)
-    const int64_t tile = static_cast<int64_t>(mt) * gridDim.x + nt;
-    float* part = p.partials + ((tile * S + s) * BN) * kTileW;
-#pragma unroll
-    for (int j = 0; j < C::kCpw; ++j) {
-      const int row = col0 + j;
-      if (m0 + row < p.M) __stcg(part + row * kTileW + n_loc, acc[j]);
-    }
-    __threadfence();
-  }
   tc_fence_before();
   __syncthreads();  // every role has left its loop: the abort flag is final from here on
   tc_fence_after();
@@ -325,45 +364,47 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
   if (S == 1) {
     if (!ok) return;
-    // Stage the bf16 tile in shared memory (the A ring is idle now: every TMA
-    // copy was consumed and every MMA reading it has completed), then write
-    // 16-byte vectors along rows of Y.
-    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffA);
-    if (is_epi) {
-#pragma unroll
-      for (int j = 0; j < C::kCpw; ++j) stg[(col0 + j) * kTileW + n_loc] = __float2bfloat16_rn(acc[j]);
-    }
-    __syncthreads();
-    const int rows = min(BN, p.M - m0);
-    const int chunks = rows * (kTileW / 8);           // 16-byte chunks
-    for (int c = threadIdx.x; c < chunks; c += kThreads) {
-      const int row = c >> 4;
-      const int cc = c & 15;
-      const uint4 v = *reinterpret_cast<const uint4*>(stg + row * kTileW + cc * 8);
-      *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m0 + row) * p.ldo + n0 + cc * 8) = v;
+    // 16-byte vectors of the staged bf16 tile along rows of Y
+    const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffA);
+    constexpr int kRowChunks = BN / 8;
+    for (int c = threadIdx.x; c < rows * kRowChunks; c += kThreads) {
+      const int r = c / kRowChunks, cc = c % kRowChunks;
+      const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
+      *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8) = v;
     }
     return;
   }
 
-  // Split-K: publish partials to the cluster (every CTA arrives, also after
-  // an abort, so no CTA of the cluster waits forever), then reduce a disjoint
-  // block of rows over the slices in fixed order.
+  // Split-K: copy the staged fp32 partial to the workspace, publish it to the
+  // cluster (every CTA arrives, also after an abort, so no CTA of the cluster
+  // waits forever), then reduce a disjoint block of rows over the slices in
+  // fixed order.
+  const int64_t tile = static_cast<int64_t>(mt) * gridDim.x + nt;
+  constexpr int kRowF4 = BN / 4;
+  if (ok) {
+    const float* stg = reinterpret_cast<const float*>(smem + C::kOffA);
+    float* part = p.partials + (tile * S + s) * kTileM * BN;
+    for (int c = threadIdx.x; c < rows * kRowF4; c += kThreads) {
+      const int r = c / kRowF4, c4 = c % kRowF4;
+      __stcg(reinterpret_cast<float4*>(part + r * BN + c4 * 4),
+             *reinterpret_cast<const float4*>(stg + r * C::kPitch32 + c4 * 4));
+    }
+    __threadfence();
+  }
   cluster_sync_all();
   if (!ok) return;
-  const int64_t tile = static_cast<int64_t>(mt) * gridDim.x + nt;
-  const float* part0 = p.partials + (tile * S) * BN * kTileW;
-  const int rows = min(BN, p.M - m0);
+  const float* part0 = p.partials + tile * S * kTileM * BN;
   const int per = (rows + S - 1) / S;
   const int r0 = s * per;
   const int r1 = min(rows, r0 + per);
-  const int items = (r1 > r0 ? r1 - r0 : 0) * (kTileW / 4);
+  const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
   for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int row = r0 + (it >> 5);
-    const int c4 = it & 31;
-    const float* src = part0 + row * kTileW + c4 * 4;
+    const int r = r0 + it / kRowF4;
+    const int c4 = it % kRowF4;
+    const float* src = part0 + r * BN + c4 * 4;
     float4 sum = __ldcg(reinterpret_cast<const float4*>(src));
     for (int t = 1; t < S; ++t) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * BN * kTileW));
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
       sum.x += v.x;
       sum.y += v.y;
       sum.z += v.z;
@@ -374,7 +415,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     uint2 pk;
     pk.x = *reinterpret_cast<uint32_t*>(&lo);
     pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(p.out + static_cast<int64_t>(m0 + row) * p.ldo + n0 + c4 * 4) = pk;
+    *reinterpret_cast<uint2*>(p.out + static_cast<int64_t>(m0 + r) * p.ldo + n0 + c4 * 4) = pk;
   }
 }
 
@@ -422,11 +463,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 constexpr int kMaxDevices = 64;
 
+constexpr int kVariants = 3;  // weight tiles 64, 128, 256
+
+static int variant(int bn) { return bn == 64 ? 0 : bn == 128 ? 1 : 2; }
+
 struct DeviceInfo {
   bool init = false;
   bool sm100 = false;
   int sms = 0;
-  unsigned configured = 0;  // bit per token-tile variant: dynamic smem attribute set
+  unsigned configured = 0;                       // bit per variant: attributes checked and set
+  int clusters[kVariants][kMaxSplit + 1] = {};   // max co-resident clusters per (variant, split); 0 = unknown
 };
 
 static std::mutex g_mu;
@@ -465,76 +511,160 @@ static int device_info(DeviceInfo** out) {
   return d.sm100 ? FACK_OK : FACK_ERR_UNSUPPORTED_ARCH;
 }
 
-// Token tile for M: one tile up to 256 tokens, else the fewest 256-wide
-// tiles, each rounded up to a multiple of 32.
-static int pick_tile_m(int M) {
-  const int tiles = (M + 255) / 256;
-  const int per = (M + tiles - 1) / tiles;
-  int bn = ((per + 31) / 32) * 32;
-  return bn < 32 ? 32 : bn;
+struct KernelEntry {
+  const void* fn;
+  int smem;
+};
+
+template <int BN>
+static KernelEntry entry() {
+  return {reinterpret_cast<const void*>(gemm_bs_kernel<BN>), Cfg<BN>::kSmemBytes};
 }
 
-// Split-K choice: the stand-in for aiter's tuned (M,N,K,cu_num) table.  Cost
-// model in units of one 128-wide K step of one CTA: waves * steps-per-CTA,
-// plus a fixed cost per extra slice for writing and re-reading the fp32
-// partial tile.  Slices keep >= 4 K steps each.
-static int pick_split(int M, int N, int K, int bn, int sms) {
+static const KernelEntry& kernel_for(int bn) {
+  static const KernelEntry table[kVariants] = {entry<64>(), entry<128>(), entry<256>()};
+  return table[variant(bn)];
+}
+
+static int ensure_configured(DeviceInfo* d, int bn) {
+  const int v = variant(bn);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!(d->configured & (1u << v))) {
+    const KernelEntry& k = kernel_for(bn);
+    // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
+    // launch; with any other count setmaxnreg.inc could wait forever, so the
+    // kernel is refused instead of launched.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, k.fn) != cudaSuccess || fa.numRegs != kLaunchRegs ||
+        fa.maxThreadsPerBlock < kThreads)
+      return FACK_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
+      return FACK_ERR_LAUNCH;
+    d->configured |= 1u << v;
+  }
+  return FACK_OK;
+}
+
+// How many clusters of `split` CTAs (or, for split 1, single CTAs) of the
+// weight-tile variant `bn` the device holds at once.  Clusters must fit inside
+// one GPC, so on B200 fewer than 148/split clusters of a size fit.
+static int co_resident(DeviceInfo* d, int bn, int split) {
+  const int v = variant(bn);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (d->clusters[v][split]) return d->clusters[v][split];
+  }
+  if (ensure_configured(d, bn) != FACK_OK) return 0;
+  const KernelEntry& k = kernel_for(bn);
+  int n = 0;
+  if (split == 1) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kThreads, k.smem) != cudaSuccess) return 0;
+    n = per_sm * d->sms;
+  } else {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(1, 1, split);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = k.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = split;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) return 0;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  d->clusters[v][split] = n;
+  return n;
+}
+
+// Plan (weight tile BN, split-K S): the stand-in for aiter's tuned
+// (M,N,K,cu_num) table.  Estimated time of a launch, in SM cycles:
+//   waves x K-steps per CTA x max(control floor, MMA, rescale)
+//   + for S > 1: fp32 partial write + re-read and the cluster barrier,
+// bounded below by the HBM time of the operands.  A wave is the number of
+// tiles the device holds at once (clusters of S CTAs must fit in one GPC).
+static double plan_cost(DeviceInfo* d, int M, int N, int K, int bn, int sp) {
   const int KB = K / kBlk;
-  const int tiles = (N / kTileW) * ((M + bn - 1) / bn);
-  int best = 1;
-  double best_cost = 1e30;
-  for (int sp = 1; sp <= kMaxSplit; ++sp) {
-    if (sp > 1 && KB / sp < 4) break;
-    const int ctas = tiles * sp;
-    const int waves = (ctas + sms - 1) / sms;
-    const int steps = (KB + sp - 1) / sp;
-    const double reduce = sp > 1 ? 2.0 + 4.0 * bn / 256.0 : 0.0;
-    const double cost = static_cast<double>(waves) * steps + reduce;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = sp;
+  const int mtiles = (M + kTileM - 1) / kTileM;
+  const int tiles = mtiles * (N / bn);
+  const int slots = co_resident(d, bn, sp);
+  if (slots <= 0) return 1e30;
+  const int waves = (tiles + slots - 1) / slots;
+  const int steps = (KB + sp - 1) / sp;
+  const int quarters = (M >= kTileM) ? 4 : (M + 31) / 32;
+  const double t_kb = fmax(fmax(450.0, 2.0 * bn), 0.45 * bn * quarters + 150.0);
+  double cyc = static_cast<double>(waves) * steps * t_kb + 2500.0;
+  if (sp > 1) cyc += 1500.0 + 2.0 * kTileM * bn * 4.0 / 96.0;
+  const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K * (N / bn);
+  const double hbm_cyc = bytes / 6.5e12 * 1.9e9;
+  return fmax(cyc, hbm_cyc);
+}
+
+// Weight tile for an explicitly requested split (no device query needed, so
+// the workspace size of an explicit split is a pure function of the shape):
+// the largest tile that still gives >= 120 CTAs, else the smallest.
+static int tile_for_split(int M, int N, int sp) {
+  const int mtiles = (M + kTileM - 1) / kTileM;
+  for (int bn : {256, 128})
+    if (N % bn == 0 && mtiles * (N / bn) * sp >= 120) return bn;
+  return 64;
+}
+
+static int plan_auto(DeviceInfo* d, int M, int N, int K, int* bn_out, int* sp_out) {
+  const int KB = K / kBlk;
+  double best = 1e30;
+  int bb = 0, bs = 0;
+  for (int bn : {256, 128, 64}) {
+    if (N % bn) continue;
+    for (int sp = 1; sp <= kMaxSplit && sp <= KB; ++sp) {
+      if (sp > 1 && KB / sp < 2) break;
+      const double c = plan_cost(d, M, N, K, bn, sp);
+      if (c < best * 0.97) {  // prefer the larger tile / smaller split unless clearly faster
+        best = c;
+        bb = bn;
+        bs = sp;
+      }
     }
   }
-  return best;
+  if (!bb) return FACK_ERR_LAUNCH;
+  *bn_out = bb;
+  *sp_out = bs;
+  return FACK_OK;
 }
 
 static size_t workspace_bytes_for(int M, int N, int bn, int split) {
   if (split <= 1) return 0;
-  const size_t tiles = static_cast<size_t>(N / kTileW) * ((M + bn - 1) / bn);
-  return tiles * split * bn * kTileW * sizeof(float);
+  const size_t tiles = static_cast<size_t>(N / bn) * ((M + kTileM - 1) / kTileM);
+  return tiles * split * kTileM * bn * sizeof(float);
 }
 
 static int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw,
+                     CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_128B) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, promo,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FACK_OK : FACK_ERR_BAD_ALIGN;
 }
 
-template <int BN>
-static int launch_bn(DeviceInfo* d, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int M,
-                     cudaStream_t stream) {
-  using C = Cfg<BN>;
-  auto kern = gemm_bs_kernel<BN>;
-  const unsigned bit = 1u << (BN / 32 - 1);
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!(d->configured & bit)) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-        return FACK_ERR_LAUNCH;
-      d->configured |= bit;
-    }
-  }
+static int launch(DeviceInfo* d, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int M,
+                  cudaStream_t stream) {
+  const int st = ensure_configured(d, bn);
+  if (st != FACK_OK) return st;
+  const KernelEntry& k = kernel_for(bn);
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(p.N / kTileW, (M + BN - 1) / BN, p.split);
+  cfg.gridDim = dim3(p.N / bn, (M + kTileM - 1) / kTileM, p.split);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.dynamicSmemBytes = k.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   cfg.attrs = attr;
@@ -546,7 +676,8 @@ static int launch_bn(DeviceInfo* d, const CUtensorMap& tw, const CUtensorMap& tx
     attr[0].val.clusterDim.z = p.split;
     cfg.numAttrs = 1;
   }
-  if (cudaLaunchKernelEx(&cfg, kern, tw, tx, p) != cudaSuccess) return FACK_ERR_LAUNCH;
+  void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tx), const_cast<Params*>(&p)};
+  if (cudaLaunchKernelExC(&cfg, k.fn, args) != cudaSuccess) return FACK_ERR_LAUNCH;
   return FACK_OK;
 }
 
@@ -576,31 +707,52 @@ const char* fack_status_string(int status) {
 
 int fack_version(void) { return 100; }
 
-int fack_gemm_bs_select(int M, int N, int K, int split_k_request, int* tile_m, int* split_k) {
-  if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
-  if (!tile_m || !split_k) return FACK_ERR_BAD_ARG;
-  const int bn = pick_tile_m(M);
+int fack_gemm_bs_plan(int M, int N, int K, int tile_n_request, int split_k_request, int* tile_n, int* split_k,
+                      size_t* workspace_bytes) {
+  if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
+  if (!tile_n || !split_k) return FACK_ERR_BAD_ARG;
   const int KB = K / kBlk;
-  int sp = split_k_request;
-  if (sp < 0 || sp > kMaxSplit || sp > KB) return FACK_ERR_BAD_ARG;
-  if (sp == 0) {
+  if (split_k_request < 0 || split_k_request > kMaxSplit || split_k_request > KB) return FACK_ERR_BAD_ARG;
+  if (tile_n_request != 0 && tile_n_request != 64 && tile_n_request != 128 && tile_n_request != 256)
+    return FACK_ERR_BAD_ARG;
+  if (tile_n_request && N % tile_n_request) return FACK_ERR_BAD_ARG;
+  int bn = tile_n_request, sp = split_k_request;
+  if (sp && !bn) {
+    bn = tile_for_split(M, N, sp);
+  } else if (!sp) {
     DeviceInfo* d = nullptr;
     const int st = device_info(&d);
     if (st != FACK_OK) return st;
-    sp = pick_split(M, N, K, bn, d->sms);
+    if (bn) {
+      double best = 1e30;
+      for (int c = 1; c <= kMaxSplit && c <= KB; ++c) {
+        if (c > 1 && KB / c < 2) break;
+        const double cost = plan_cost(d, M, N, K, bn, c);
+        if (cost < best * 0.97) {
+          best = cost;
+          sp = c;
+        }
+      }
+      if (!sp) return FACK_ERR_LAUNCH;
+    } else {
+      const int st2 = plan_auto(d, M, N, K, &bn, &sp);
+      if (st2 != FACK_OK) return st2;
+    }
   }
-  *tile_m = bn;
+  *tile_n = bn;
   *split_k = sp;
+  if (workspace_bytes) *workspace_bytes = workspace_bytes_for(M, N, bn, sp);
   return FACK_OK;
+}
+
+int fack_gemm_bs_select(int M, int N, int K, int split_k_request, int* tile_n, int* split_k) {
+  return fack_gemm_bs_plan(M, N, K, 0, split_k_request, tile_n, split_k, nullptr);
 }
 
 int fack_gemm_bs_workspace_size(int M, int N, int K, int split_k, size_t* bytes) {
   if (!bytes) return FACK_ERR_BAD_ARG;
   int bn = 0, sp = 0;
-  const int st = fack_gemm_bs_select(M, N, K, split_k, &bn, &sp);
-  if (st != FACK_OK) return st;
-  *bytes = workspace_bytes_for(M, N, bn, sp);
-  return FACK_OK;
+  return fack_gemm_bs_plan(M, N, K, 0, split_k, &bn, &sp, bytes);
 }
 
 int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, int N, int K, void* wq_packed,
@@ -628,9 +780,9 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, in
   return FACK_OK;
 }
 
-int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
-                 int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
-                 int N, int K, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
+int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                    int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
+                    int N, int K, int tile_n, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
   if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
   if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
@@ -644,19 +796,20 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, con
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != FACK_OK) return st;
-  const int bn = pick_tile_m(M);
-  const int sp = split_k ? split_k : pick_split(M, N, K, bn, d->sms);
-  const size_t need = workspace_bytes_for(M, N, bn, sp);
+  int bn = 0, sp = 0;
+  size_t need = 0;
+  st = fack_gemm_bs_plan(M, N, K, tile_n, split_k, &bn, &sp, &need);
+  if (st != FACK_OK) return st;
   if (need && (!workspace || workspace_bytes < need || !aligned(workspace, 16))) return FACK_ERR_WS_TOO_SMALL;
 
   CUtensorMap tw, tx;
   if (wq_packed == FACK_W_PACKED)
-    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk, kTileW,
-                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk, bn < kBlk ? bn : kBlk,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);  // packed tiles are contiguous
   else
-    st = encode_2d(&tw, wq, K, N, K, kBlk, kTileW, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_2d(&tw, wq, K, N, K, kBlk, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
-  st = encode_2d(&tx, xq, K, M, ldx, kBlk, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  st = encode_2d(&tx, xq, K, M, ldx, kBlk, kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
 
   Params p;
@@ -676,17 +829,14 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, con
   p.timeout_ns = 2000000000ull;  // 2 s: far above any legitimate wait, short enough to report a lost arrival
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (bn) {
-    case 32: return launch_bn<32>(d, tw, tx, p, M, s);
-    case 64: return launch_bn<64>(d, tw, tx, p, M, s);
-    case 96: return launch_bn<96>(d, tw, tx, p, M, s);
-    case 128: return launch_bn<128>(d, tw, tx, p, M, s);
-    case 160: return launch_bn<160>(d, tw, tx, p, M, s);
-    case 192: return launch_bn<192>(d, tw, tx, p, M, s);
-    case 224: return launch_bn<224>(d, tw, tx, p, M, s);
-    case 256: return launch_bn<256>(d, tw, tx, p, M, s);
-    default: return FACK_ERR_BAD_ARG;
-  }
+  return launch(d, bn, tw, tx, p, M, s);
+}
+
+int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                 int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
+                 int N, int K, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
+  return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, 0,
+                         split_k, workspace, workspace_bytes, stream);
 }
 
 int fack_gather_interleave(const void* gathered, int g, int M, int n_shard, void* out, int64_t ldo, void* stream) {

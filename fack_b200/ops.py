@@ -39,6 +39,7 @@ CUDA-graph capture, so a warmed-up call is capturable.
 from __future__ import annotations
 
 import ctypes
+import re
 from typing import Optional
 
 import torch
@@ -67,26 +68,40 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
-def kernel_name(tile_m: int, split_k: int) -> str:
-    return f"{KERNEL_PREFIX}_t{tile_m}x128_s{split_k}"
+def kernel_name(tile_n: int, split_k: int) -> str:
+    return f"{KERNEL_PREFIX}_t128x{tile_n}_s{split_k}"
+
+
+def parse_kernel_name(name) -> tuple:
+    """(tile_n, split_k) encoded in one of this library's kernel names, else (0, 0).
+
+    The reviewed gfx942 symbols name AMD code objects and carry no tile that
+    applies here, so they (and None / "") leave the choice to the library."""
+    if not name or name in AITER_SYMBOLS:
+        return 0, 0
+    m = re.fullmatch(KERNEL_PREFIX + r"_t128x(64|128|256)_s([1-8])", str(name))
+    if not m:
+        raise ValueError(f"unknown blockscale kernel {name!r}")
+    return int(m.group(1)), int(m.group(2))
+
+
+def plan(M: int, N: int, K: int, tile_n: int = 0, split_k: int = 0) -> tuple:
+    """(tile_n, split_k, workspace_bytes) the library uses; 0 = library choice."""
+    lib = _lib.load()
+    tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    _lib.check(lib.fack_gemm_bs_plan(int(M), int(N), int(K), int(tile_n), int(split_k), ctypes.byref(tn),
+                                     ctypes.byref(sk), ctypes.byref(nb)), "fack_gemm_bs_plan")
+    return tn.value, sk.value, nb.value
 
 
 def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     """Kernel and split-K this library uses for (M, N, K) on the current device."""
-    lib = _lib.load()
-    tm, sk = ctypes.c_int(), ctypes.c_int()
-    _lib.check(lib.fack_gemm_bs_select(int(M), int(N), int(K), int(split_k), ctypes.byref(tm),
-                                       ctypes.byref(sk)), "fack_gemm_bs_select")
-    return {"libtype": "asm", "kernelName": kernel_name(tm.value, sk.value), "splitK": sk.value,
-            "tile_m": tm.value, "tile_n": BLOCK}
+    tn, sk, _ = plan(M, N, K, 0, split_k)
+    return {"libtype": "asm", "kernelName": kernel_name(tn, sk), "splitK": sk, "tile_m": 128, "tile_n": tn}
 
 
-def workspace_size(M: int, N: int, K: int, split_k: int = 0) -> int:
-    lib = _lib.load()
-    nb = ctypes.c_size_t()
-    _lib.check(lib.fack_gemm_bs_workspace_size(int(M), int(N), int(K), int(split_k), ctypes.byref(nb)),
-               "fack_gemm_bs_workspace_size")
-    return nb.value
+def workspace_size(M: int, N: int, K: int, split_k: int = 0, tile_n: int = 0) -> int:
+    return plan(M, N, K, tile_n, split_k)[2]
 
 
 def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
@@ -125,24 +140,24 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
         raise ValueError("all tensors must be on one device")
 
 
-def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k):
+def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_n=0):
     M, K = xq.shape
     N = wq.shape[0]
     dev = xq.device
     lib = _lib.load()
     with torch.cuda.device(dev):
-        need = workspace_size(M, N, K, split_k)
+        tn, sk, need = plan(M, N, K, tile_n, split_k)
         ws = _workspace(dev, need)
-        st = lib.fack_gemm_bs(
+        st = lib.fack_gemm_bs_ex(
             xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
             x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0),
-            M, N, K, int(split_k), _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
-    _lib.check(st, "fack_gemm_bs")
+            M, N, K, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
+    _lib.check(st, "fack_gemm_bs_ex")
     return out
 
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
-                    out: Optional[torch.Tensor] = None, split_k: int = 0) -> torch.Tensor:
+                    out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0) -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
@@ -162,7 +177,7 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
         sk = max(sk, 1)
     if M == 1:
         sm = max(sm, 1)
-    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k)
+    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_n)
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):
@@ -182,15 +197,15 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     ``bias`` must be None: the blockscale operator has no bias term
     (client/aiter/hsa/gfx942/dispatch_driver.py:66-67); ``zero_bias_buf`` is
     accepted and unused.  ``kernelName`` may be None, one of the reviewed
-    gfx942 symbols or one of this library's names; ``splitK`` None/0 lets the
-    library choose.  ``bpreshuffle=True`` requires ``b`` from
+    gfx942 symbols (library choice of tile) or one of this library's names
+    ``fack_bs_sm100_t128x{64|128|256}_s{1..8}``, which fixes the weight tile
+    (and the split, unless ``splitK`` is given); ``splitK`` None/0 otherwise
+    lets the library choose.  ``bpreshuffle=True`` requires ``b`` from
     :func:`shuffle_weight`.
     """
     if bias is not None:
         raise ValueError("the blockscale operator takes no bias")
-    if kernelName not in (None, "") and kernelName not in AITER_SYMBOLS and not str(kernelName).startswith(
-            KERNEL_PREFIX):
-        raise ValueError(f"unknown blockscale kernel {kernelName!r}")
+    tile_n, name_split = parse_kernel_name(kernelName)
     shuffled = bool(getattr(b, "is_shuffled", False))
     if bool(bpreshuffle) != shuffled:
         raise ValueError("bpreshuffle={} but the weight {} a shuffle_weight() output".format(
@@ -201,8 +216,8 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     N = b.shape[0]
     _check_common(a, b, w_scale, out, M, N, K)
     sm, sk = _aiter_xscale_strides(x_scale, M, K // BLOCK)
-    split = 0 if splitK is None else int(splitK)
-    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split)
+    split = name_split if splitK is None else int(splitK)
+    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_n)
 
 
 def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bfloat16):

@@ -59,15 +59,28 @@ const char* fack_status_string(int status);
 int fack_version(void);
 
 /*
- * Tile / split-K plan the library uses for an (M,N,K) problem on the current
- * device.  split_k_request = 0 asks for the library's own choice (the stand-in
- * for aiter's tuned-CSV lookup get_CKGEMM_config, see
- * client/aiter/dispatch.py:23-35 and unittests/test_aiter_dispatch.py:472-477);
- * a positive value is validated and echoed.  tile_m receives the token tile
- * (UMMA N extent), split_k the number of K slices.
+ * Full plan: weight-tile width (64, 128 or 256; 0 = library choice) and split-K
+ * (1..8; 0 = library choice) for an (M,N,K) problem, with the workspace bytes
+ * fack_gemm_bs_ex needs for that plan (0 for a single K slice).  A library
+ * choice of either value queries the current device (cluster occupancy); a
+ * fully explicit request does not.  Plays the role of aiter's per-shape
+ * kernelName/splitK selection (client/aiter/dispatch.py:142-150).
+ */
+int fack_gemm_bs_plan(int M, int N, int K, int tile_n_request, int split_k_request,
+                      int* tile_n, int* split_k, size_t* workspace_bytes);
+
+/*
+ * Tile / split-K plan the library uses for an (M,N,K) problem.  Every CTA
+ * computes a 128-token x tile_n-weight-row block of Y (tile_n = 64, 128 or
+ * 256) over split_k slices of K.  split_k_request = 0 asks for the library's
+ * own choice on the current device (the stand-in for aiter's tuned-CSV lookup
+ * get_CKGEMM_config, client/aiter/dispatch.py:23-35 and
+ * unittests/test_aiter_dispatch.py:472-477); a positive value is validated,
+ * echoed, and paired with a tile chosen from the shape alone (no device
+ * query).
  */
 int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
-                        int* tile_m, int* split_k);
+                        int* tile_n, int* split_k);
 
 /*
  * Bytes of workspace fack_gemm_bs needs for this problem and split (0 when the
@@ -120,6 +133,17 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                  const float* w_scale, void* out, int64_t ldo,
                  int M, int N, int K, int split_k,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * fack_gemm_bs with an explicit weight-tile width tile_n (0 = library choice),
+ * the counterpart of aiter selecting one tile kernel by kernelName
+ * (client/aiter/hsa/gfx942/driver.py:26-29 passes kernelName=symbol).
+ */
+int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
+                    const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,
+                    const float* w_scale, void* out, int64_t ldo,
+                    int M, int N, int K, int tile_n, int split_k,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Column interleave for the N-sharded multi-GPU path: `gathered` holds g

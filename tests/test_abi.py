@@ -52,21 +52,24 @@ def test_bad_shapes_rejected(m, n, k):
 
 def test_explicit_split_plan_and_workspace_without_device():
     lib = _lib.load()
-    tm, sk = ctypes.c_int(), ctypes.c_int()
-    assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tm), ctypes.byref(sk)) == 0
-    assert (tm.value, sk.value) == (256, 6)
-    assert lib.fack_gemm_bs_select(1, 3072, 7168, 1, ctypes.byref(tm), ctypes.byref(sk)) == 0
-    assert tm.value == 32
-    assert lib.fack_gemm_bs_select(300, 3072, 7168, 1, ctypes.byref(tm), ctypes.byref(sk)) == 0
-    assert tm.value == 160  # two token tiles of 150 -> 160
+    tn, sk = ctypes.c_int(), ctypes.c_int()
+    # 2 token tiles x 12 weight tiles of 256 x 6 slices = 144 CTAs -> 256-row weight tiles
+    assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tn), ctypes.byref(sk)) == 0
+    assert (tn.value, sk.value) == (256, 6)
+    # one token tile x 12 tiles = too few CTAs for 256 or 128 at split 1 -> 64-row tiles
+    assert lib.fack_gemm_bs_select(1, 3072, 7168, 1, ctypes.byref(tn), ctypes.byref(sk)) == 0
+    assert tn.value == 64
+    # N = 384 is not a multiple of 256
+    assert lib.fack_gemm_bs_select(300, 384, 7168, 8, ctypes.byref(tn), ctypes.byref(sk)) == 0
+    assert tn.value in (64, 128)
     nb = ctypes.c_size_t()
     assert lib.fack_gemm_bs_workspace_size(256, 3072, 7168, 6, ctypes.byref(nb)) == 0
-    assert nb.value == 24 * 6 * 256 * 128 * 4
+    assert nb.value == (2 * 12) * 6 * 128 * 256 * 4
     assert lib.fack_gemm_bs_workspace_size(256, 3072, 7168, 1, ctypes.byref(nb)) == 0
     assert nb.value == 0
     # split beyond the cluster limit or beyond K/128 is refused
-    assert lib.fack_gemm_bs_select(256, 3072, 7168, 9, ctypes.byref(tm), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
-    assert lib.fack_gemm_bs_select(256, 3072, 256, 3, ctypes.byref(tm), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs_select(256, 3072, 7168, 9, ctypes.byref(tn), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs_select(256, 3072, 256, 3, ctypes.byref(tn), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
 
 
 def test_pointer_and_stride_checks_before_device():

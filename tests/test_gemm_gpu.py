@@ -55,14 +55,20 @@ def test_golden_through_reference_call_form(cuda_device, name):
 
 @pytest.mark.parametrize("name", golden_names())
 @pytest.mark.parametrize("packed", [False, True])
-def test_golden_every_split(cuda_device, name, packed):
+def test_golden_every_tile_and_split(cuda_device, name, packed):
+    """Every weight-tile variant (selected by kernelName, as aiter selects its
+    tile kernels) at every split-K the shape allows."""
     g = golden_on(name, cuda_device)
     b = fb.shuffle_weight(g["b"]) if packed else g["b"]
-    for split in range(1, min(8, g["k"] // 128) + 1):
-        out = poisoned(g["m"], g["n"], cuda_device)
-        fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=split,
-                                                bpreshuffle=packed)
-        assert_close(out, g["reference"], f"{name} split={split} packed={packed}")
+    for tile in (64, 128, 256):
+        if g["n"] % tile:
+            continue
+        for split in range(1, min(8, g["k"] // 128) + 1):
+            out = poisoned(g["m"], g["n"], cuda_device)
+            fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=split,
+                                                    kernelName=f"fack_bs_sm100_t128x{tile}_s{split}",
+                                                    bpreshuffle=packed)
+            assert_close(out, g["reference"], f"{name} tile={tile} split={split} packed={packed}")
 
 
 @pytest.mark.parametrize("name", golden_names())
