@@ -23,6 +23,7 @@ FACK_ERR_UNSUPPORTED_ARCH = 6
 FACK_ERR_BAD_ARG = 7
 FACK_ERR_DEVICE_TIMEOUT = 8
 FACK_ERR_CUDA = 9
+FACK_ERR_SCRATCH_LIMIT = 10
 
 FACK_W_ROW_MAJOR = 0
 FACK_W_PACKED = 1
@@ -42,6 +43,8 @@ SIGNATURES = {
     "fack_gemm_bs_prepack_w": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p]),
     "fack_gemm_bs": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                               _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
+    "fack_gemm_bs_noalloc": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
+                                      _c_int, _c_int, _c_int, _c_int, _c_p]),
     "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
 }

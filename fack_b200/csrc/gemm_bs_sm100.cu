@@ -683,6 +683,32 @@ static int launch(DeviceInfo* d, int bn, const CUtensorMap& tw, const CUtensorMa
 
 static bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
 
+// ------------------------------------------------------ no-alloc scratch --
+// Split-K scratch for fack_gemm_bs_noalloc: part of the library's own device
+// image, so it exists on every GPU that loads the library, from load until the
+// process exits, and using it never allocates.  16 MiB covers the decode
+// shapes up to M = 512 at N = 3072 with the library's own split choice.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+static void* g_noalloc_ptr[kMaxDevices];  // device address of the buffer, resolved once per device
+
+// The array's name in host code is only a host-side handle: its device
+// address must be asked for, on the device in question, before a kernel may
+// use it.  The first call on each device does that (a runtime query, not an
+// allocation) and caches the answer.
+static int noalloc_scratch(void** out) {
+  int dev;
+  if (current_device(&dev) != FACK_OK) return FACK_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return FACK_ERR_CUDA;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FACK_OK;
+}
+
 }  // namespace fack
 
 using namespace fack;
@@ -701,6 +727,9 @@ const char* fack_status_string(int status) {
     case FACK_ERR_BAD_ARG: return "invalid argument";
     case FACK_ERR_DEVICE_TIMEOUT: return "a kernel gave up on a bounded wait (device status set)";
     case FACK_ERR_CUDA: return "CUDA runtime query failed";
+    case FACK_ERR_SCRATCH_LIMIT:
+      return "problem needs more split-K scratch than the no-allocation entry point's built-in 16 MiB; "
+             "use fack_gemm_bs with a caller-owned workspace or request a smaller split_k";
     default: return "unknown status";
   }
 }
@@ -837,6 +866,24 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, con
                  int N, int K, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
   return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, 0,
                          split_k, workspace, workspace_bytes, stream);
+}
+
+int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                         int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                         int M, int N, int K, int split_k, void* stream) {
+  int bn = 0, sp = 0;
+  size_t need = 0;
+  int st = fack_gemm_bs_plan(M, N, K, 0, split_k, &bn, &sp, &need);
+  if (st != FACK_OK) return st;
+  if (need > kNoAllocScratchBytes) return FACK_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (need) {
+    st = noalloc_scratch(&scratch);
+    if (st != FACK_OK) return st;
+  }
+  // The same kernel and plan as fack_gemm_bs; only the workspace differs.
+  return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, bn,
+                         sp, scratch, need ? kNoAllocScratchBytes : 0, stream);
 }
 
 int fack_gather_interleave(const void* gathered, int g, int M, int n_shard, void* out, int64_t ldo, void* stream) {

@@ -43,7 +43,8 @@ enum fack_status {
   FACK_ERR_UNSUPPORTED_ARCH = 6,/* current device is not sm_100 */
   FACK_ERR_BAD_ARG = 7,         /* other invalid argument (split_k, layout, g) */
   FACK_ERR_DEVICE_TIMEOUT = 8,  /* a kernel gave up waiting (device status) */
-  FACK_ERR_CUDA = 9             /* a CUDA runtime query failed */
+  FACK_ERR_CUDA = 9,            /* a CUDA runtime query failed */
+  FACK_ERR_SCRATCH_LIMIT = 10   /* fack_gemm_bs_noalloc: built-in scratch too small */
 };
 
 /* Weight layouts accepted by fack_gemm_bs (argument `wq_packed`). */
@@ -144,6 +145,33 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                     const float* w_scale, void* out, int64_t ldo,
                     int M, int N, int K, int tile_n, int split_k,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * fack_gemm_bs without a workspace argument, for callers that cannot allocate
+ * device memory when they call the GEMM: an engine plugin whose enqueue path
+ * must neither allocate nor synchronise (cudaMalloc may synchronise the
+ * device), code that runs inside a CUDA stream capture, or a process whose
+ * device memory is wholly owned by another allocator.  No counterpart in the
+ * reference (aiter's launcher allocates its own buffers).
+ *
+ * The split-K partial sums go to one 16 MiB buffer compiled into this library
+ * (every GPU that loads the library keeps it until the process exits).
+ * Problems whose plan needs more return FACK_ERR_SCRATCH_LIMIT before
+ * anything is launched; a smaller split_k, or fack_gemm_bs with your own
+ * workspace, avoids that.  Nothing in the buffer has to start at zero: each
+ * call writes every partial it later reads.
+ *
+ * The buffer is shared by all calls on a device and keeps the last call's
+ * contents, so calls whose kernels may overlap on the GPU (for example on
+ * two streams without an ordering between them) race and corrupt each other;
+ * order them on one stream.  The first call on each device looks up the
+ * buffer's device address (a runtime query, no allocation): make that first
+ * call before any stream capture.  It calls no cudaMalloc or cudaFree.
+ */
+int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_packed,
+                         const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,
+                         const float* w_scale, void* out, int64_t ldo,
+                         int M, int N, int K, int split_k, void* stream);
 
 /*
  * Column interleave for the N-sharded multi-GPU path: `gathered` holds g
