@@ -152,21 +152,24 @@ def make_sets(wl, n_sets, dev, shard):
     return sets
 
 
-def capture(fn_steps, stream):
+def capture(fn_steps, stream, keep):
+    """Capture fn_steps() into a CUDA graph (kept in `keep`); returns its replay."""
     g = torch.cuda.CUDAGraph()
+    keep.append(g)
     with torch.cuda.graph(g, stream=stream):
         fn_steps()
-    return g
+    return g.replay
 
 
-def timed_graph_replay(graphs, stream):
-    """Replay [(graph, times)], bracketed by CUDA events on `stream`; ms."""
+def timed_graph_replay(plan, stream):
+    """Run [(fn, times)] (graph replays or eager step loops), bracketed by CUDA
+    events on `stream`; ms."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):  # replay() launches on the current stream
+    with torch.cuda.stream(stream):  # replay() and eager launches use the current stream
         start.record(stream)
-        for g, times in graphs:
+        for fn, times in plan:
             for _ in range(times):
-                g.replay()
+                fn()
         end.record(stream)
     end.synchronize()
     return start.elapsed_time(end)
@@ -234,7 +237,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=90), device_id=dev)
     wl = data.WORKLOADS[args.workload]
     sharded = args.workload in SHARDED and world > 1
     shard = (rank, world) if sharded else None
@@ -262,6 +265,7 @@ def run_ours(args):
         else:
             gemm_call(s)
 
+    log(f"[bench rank {rank}] {wl.name}: {n_sets} input sets, plan {cfg['kernelName']}, sharded={sharded}")
     # warm-up (eager: sizes the split-K workspace and the gather buffer)
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -270,21 +274,51 @@ def run_ours(args):
 
     chunk = max(n_sets, (min(args.steps, 1024) // n_sets) * n_sets)
     full, rem = divmod(args.steps, chunk)
-    with torch.cuda.stream(stream):
-        g_chunk = capture(lambda: [step(i) for i in range(chunk)], stream) if full else None
-        g_rem = capture(lambda: [step(i) for i in range(rem)], stream) if rem else None
-        g_gemm = None
-        if sharded:  # GEMM-only graph for the kernel roofline
-            g_gemm = capture(lambda: [gemm_call(sets[i % n_sets]) for i in range(chunk)], stream)
-    plan = [(g_chunk, full)] if full else []
+    graphs = []
+    timing = "CUDA-graph replay"
+
+    def steps_fn(n):
+        return lambda: [step(i) for i in range(n)]
+
+    def gemm_fn(n):
+        return lambda: [gemm_call(sets[i % n_sets]) for i in range(n)]
+
+    try:
+        with torch.cuda.stream(stream):
+            run_chunk = capture(steps_fn(chunk), stream, graphs) if full else None
+            run_rem = capture(steps_fn(rem), stream, graphs) if rem else None
+            run_gemm = capture(gemm_fn(chunk), stream, graphs) if sharded else None  # GEMM-only: kernel roofline
+    except Exception as e:  # collectives that cannot be captured: time eager launches instead
+        log(f"graph capture failed ({e}); timing eager launches")
+        for g in graphs:
+            g.reset()
+        graphs = []
+        timing = "eager launches"
+        run_chunk, run_rem = steps_fn(chunk), steps_fn(rem)
+        run_gemm = gemm_fn(chunk) if sharded else None
+    if world > 1:  # all ranks must time the same way (captured steps hold collectives)
+        flag = torch.tensor([1 if graphs else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if flag.item() == 0 and graphs:
+            for g in graphs:
+                g.reset()
+            graphs = []
+            timing = "eager launches"
+            run_chunk, run_rem = steps_fn(chunk), steps_fn(rem)
+            run_gemm = gemm_fn(chunk) if sharded else None
+    log(f"[bench rank {rank}] timing via {timing}")
+    plan = [(run_chunk, full)] if full else []
     if rem:
-        plan.append((g_rem, 1))
+        plan.append((run_rem, 1))
 
     # keep the GPU busy ~0.3 s before timing so clocks are sampled under load
     sampler = ClockSampler(local)
     sampler.start()
-    probe = g_chunk or g_rem
-    t_probe = timed_graph_replay([(probe, 1)], stream) / 1e3
+    probe = run_chunk or run_rem
+    # every rank must replay the same number of steps (the sharded steps hold
+    # collectives), so the warm-up count comes from the slowest rank's probe
+    t_probe = max_over_ranks(timed_graph_replay([(probe, 1)], stream) / 1e3, world, dev)
+    log(f"[bench rank {rank}] probe {t_probe * 1e3:.3f} ms per chunk; warming, then timing {args.steps} steps")
     timed_graph_replay([(probe, max(1, int(0.3 / max(t_probe, 1e-6))))], stream)
     barrier(world)
     ms = timed_graph_replay(plan, stream)
@@ -299,7 +333,7 @@ def run_ours(args):
 
     # roofline of the GEMM kernel (per launch on one GPU)
     if sharded:
-        k_ms = timed_graph_replay([(g_gemm, 1)], stream)
+        k_ms = timed_graph_replay([(run_gemm, 1)], stream)
         k_us = max_over_ranks(k_ms * 1e3 / chunk, world, dev)
     else:
         k_us = us_call
@@ -346,7 +380,7 @@ def run_ours(args):
                    "kernel": cfg["kernelName"], "weights": "prepacked (bpreshuffle=True)",
                    "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB = {n_sets * set_bytes / 1e6:.0f} MB"
                          f" (> 126 MB L2)",
-                   "timing": "CUDA-graph replay, CUDA events on the launch stream, max over ranks",
+                   "timing": f"{timing}, CUDA events on the launch stream, max over ranks",
                    "parallelism": (f"N-shard g={world} + NCCL all-gather" if sharded else
                                    ("single GPU" if world == 1 else f"{world} independent replicas"))},
         "us_per_call": round(us_call, 3), "hbm_gbs": round(data.algorithmic_bytes(wl.M, n_local, wl.K) /
@@ -359,7 +393,9 @@ def run_ours(args):
     status = fb.device_status()
     if status:
         log(f"device status flags set: {status:#x}")
-    del g_chunk, g_rem, g_gemm, plan, probe
+    for g in graphs:  # graphs holding NCCL work must go before the process group
+        g.reset()
+    del graphs, plan, probe, run_chunk, run_rem, run_gemm
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()

@@ -33,13 +33,14 @@ _c_int, _c_i64, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, cty
 SIGNATURES = {
     "fack_status_string": (ctypes.c_char_p, [_c_int]),
     "fack_version": (_c_int, []),
+    "fack_last_error": (ctypes.c_char_p, []),
     "fack_gemm_bs_select": (_c_int, [_c_int, _c_int, _c_int, _c_int,
                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "fack_gemm_bs_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_sz)]),
-    "fack_gemm_bs_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int),
-                                   ctypes.POINTER(_c_int), ctypes.POINTER(_c_sz)]),
+    "fack_gemm_bs_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int),
+                                   ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_sz)]),
     "fack_gemm_bs_ex": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
-                                 _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
+                                 _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
     "fack_gemm_bs_prepack_w": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p]),
     "fack_gemm_bs": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                               _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
@@ -81,7 +82,8 @@ class FackError(RuntimeError):
 
     def __init__(self, code: int, what: str):
         self.code = int(code)
-        super().__init__(f"{what}: {status_string(code)} (status {code})")
+        detail = load().fack_last_error().decode()
+        super().__init__(f"{what}: {status_string(code)} (status {code})" + (f" [{detail}]" if detail else ""))
 
 
 def check(code: int, what: str) -> None:

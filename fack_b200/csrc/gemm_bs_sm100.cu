@@ -39,6 +39,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <string.h>
 
 #include <mutex>
@@ -61,7 +62,7 @@ constexpr int kSmemBudget = 196608;
 // gives registers back and warpgroups 1-2 take them.  Per scheduler: one
 // control warp + two rescale warps = kCtrlRegs + 2 * kEpiRegs <= 3 * kLaunchRegs.
 constexpr int kLaunchRegs = 168;
-constexpr int kCtrlRegs = 64;
+constexpr int kCtrlRegs = 72;
 constexpr int kEpiRegs = 216;
 static_assert(kCtrlRegs + 2 * kEpiRegs <= 3 * kLaunchRegs, "register split exceeds the launch allocation");
 static_assert(kCtrlRegs % 8 == 0 && kEpiRegs % 8 == 0, "setmaxnreg counts are multiples of 8");
@@ -76,11 +77,12 @@ enum : unsigned int {
   kStDrain = 16u
 };
 
-template <int BN>
+template <int BN, bool PAIR>
 struct Cfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "weight tile must be 64, 128 or 256 rows");
+  static constexpr int kWRows = PAIR ? BN / 2 : BN;         // weight rows this CTA loads per K block
   static constexpr int kABytes = kTileM * kBlk;             // 16 KB token tile
-  static constexpr int kBBytes = BN * kBlk;                 // weight tile
+  static constexpr int kBBytes = kWRows * kBlk;             // weight tile (this CTA's part)
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
   static constexpr int kTmemBufs = (512 / BN) > 4 ? 4 : (512 / BN);
@@ -88,7 +90,8 @@ struct Cfg {
   static constexpr int kCpw = BN / 2;                       // columns per rescale warp
   static constexpr int kPitch32 = BN + 4;                   // fp32 staging pitch (floats)
   static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
-  // shared-memory carve-up (offsets from a 1024-byte aligned base)
+  // shared-memory carve-up (offsets from a 1024-byte aligned base); both CTAs
+  // of a pair use identical offsets, which the pair MMA relies on
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kStages * kABytes;
   static constexpr int kOffRaw = kOffB + kStages * kBBytes;                 // prefetched x_scale [kPrefetch][256]
@@ -108,18 +111,90 @@ struct Params {
   const float* w_scale;        // [N/128][K/128]
   __nv_bfloat16* out;
   int64_t ldo;
-  float* partials;             // [tiles][S][128][BN] fp32, S > 1 only
+  float* partials;             // [tiles][S][128][BN] fp32 for S > 1; NULL = reduce through DSMEM
   int M, N, K, KB;
   int split;
   int w_packed;
   uint64_t timeout_ns;
 };
 
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float4& v) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+  uint2 pk;
+  pk.x = *reinterpret_cast<uint32_t*>(&lo);
+  pk.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(dst) = pk;
+}
+
+// Split-K reduction over distributed shared memory: rows [r0, r1) of the
+// tile, summed over the S cluster CTAs' staged fp32 partials in rank order.
+// Kept out of line so its registers are allocated apart from the rescale loop.
+template <int BN, int PITCH>
+__device__ __noinline__ void reduce_dsmem(uint32_t stg, int S, int rank0, int rank_step, int r0, int r1,
+                                          __nv_bfloat16* out, int64_t ldo) {
+  constexpr int kRowF4 = BN / 4;
+  const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
+  for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int r = r0 + it / kRowF4;
+    const int c4 = it % kRowF4;
+    const uint32_t addr = stg + static_cast<uint32_t>((r * PITCH + c4 * 4) * 4);
+    float4 sum = dsmem_ld4(dsmem_map(addr, rank0));
+    for (int t = 1; t < S; ++t) {
+      const float4 v = dsmem_ld4(dsmem_map(addr, rank0 + t * rank_step));
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    store_bf16x4(out + r * ldo + c4 * 4, sum);
+  }
+}
+
+// Copy the staged fp32 partial (valid rows) to its workspace slot.
+template <int BN, int PITCH>
+__device__ __noinline__ void copy_partial(const float* stg, int rows, float* part) {
+  constexpr int kRowF4 = BN / 4;
+  for (int c = threadIdx.x; c < rows * kRowF4; c += kThreads) {
+    const int r = c / kRowF4, c4 = c % kRowF4;
+    __stcg(reinterpret_cast<float4*>(part + r * BN + c4 * 4),
+           *reinterpret_cast<const float4*>(stg + r * PITCH + c4 * 4));
+  }
+}
+
+// Split-K reduction from the workspace: rows [r0, r1), slices in order.
 template <int BN>
+__device__ __noinline__ void reduce_global(const float* part0, int S, int r0, int r1, __nv_bfloat16* out,
+                                           int64_t ldo) {
+  constexpr int kRowF4 = BN / 4;
+  const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
+  for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int r = r0 + it / kRowF4;
+    const int c4 = it % kRowF4;
+    const float* src = part0 + r * BN + c4 * 4;
+    float4 sum = __ldcg(reinterpret_cast<const float4*>(src));
+    for (int t = 1; t < S; ++t) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    store_bf16x4(out + r * ldo + c4 * 4, sum);
+  }
+}
+
+// PAIR = false: one CTA per 128-token x BN-weight-row tile (cta_group::1).
+// PAIR = true : two CTAs (cluster x pair) share a 256-token x BN tile through
+//   tcgen05 cta_group::2: each CTA loads its own 128 tokens and half of the
+//   BN weight rows, the even-ranked CTA (leader) issues the M=256 MMA, and
+//   each CTA receives its 128 x BN accumulator rows in its own TMEM.  Weight
+//   bytes per CTA halve; the rescale / epilogue code is the same.
+template <int BN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -128,18 +203,32 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int nt = blockIdx.x;                 // weight tile (BN output columns)
-  const int mt = blockIdx.y;                 // token tile (128 output rows)
-  const int s = blockIdx.z;                  // K slice
+  // grid: single CTAs (x = weight tile, y = token tile); pairs (x = token
+  // tile, so that the pair lies along the cluster's x dimension, y = weight
+  // tile); z = K slice
+  const int nt = PAIR ? blockIdx.y : blockIdx.x;   // weight tile (BN output columns)
+  const int mt = PAIR ? blockIdx.x : blockIdx.y;   // token tile (128 output rows)
+  const int s = blockIdx.z;                        // K slice
   const int S = p.split;
   const int m0 = mt * kTileM;
   const int n0 = nt * BN;
   const int kb0 = (s * p.KB) / S;
   const int kb1 = ((s + 1) * p.KB) / S;
   const int nk = kb1 - kb0;
-  const int rows = min(kTileM, p.M - m0);    // valid tokens in this tile (>= 1)
-  const int quarters = (rows + 31) >> 5;     // TMEM lane quarters holding valid tokens
-  const int active_warps = 2 * quarters;     // rescale warps with work
+  const int rows = min(kTileM, p.M - m0);    // valid tokens in this tile (may be <= 0 for a pair's second CTA)
+  const int quarters = rows > 0 ? (rows + 31) >> 5 : 0;   // TMEM lane quarters holding valid tokens
+  // pair bookkeeping: cluster dims (2, 1, S), rank = (mt & 1) + 2 * s
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = !PAIR || (mt & 1) == 0;
+  const uint32_t leader_rank = crank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);
+  // rescale warps that release each TMEM buffer: this CTA's (and, in a pair,
+  // the other CTA's) warps whose lane quarter holds valid tokens
+  int release_warps = 2 * quarters;
+  if (PAIR) {
+    const int other = min(kTileM, p.M - (m0 ^ kTileM));  // the other CTA's token tile: mt ^ 1
+    release_warps = 2 * ((rows > 0 ? (rows + 31) >> 5 : 0) + (other > 0 ? (other + 31) >> 5 : 0));
+  }
 
   const uint32_t bar0 = base + C::kOffBar;
   auto bar_full = [&](int i) { return bar0 + 8u * i; };
@@ -157,7 +246,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
     for (int i = 0; i < C::kTmemBufs; ++i) {
       mbar_init(bar_tfull(i), 1);
-      mbar_init(bar_tempty(i), active_warps);
+      mbar_init(bar_tempty(i), release_warps > 0 ? release_warps : 1);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -168,12 +257,25 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     prefetch_tmap(&tmap_x);
   }
   if (warp == 1) {
-    tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync_all();  // both CTAs' barriers are initialised before either signals the other's
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
+  // Everything above touches only this CTA's own resources, so with
+  // programmatic dependent launch it overlaps the previous kernel's tail;
+  // nothing the previous kernel may have written is read before this wait.
+  grid_dependency_wait();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t tmo = p.timeout_ns;
   unsigned int* status = &g_status;
@@ -188,32 +290,47 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       if (lane == 0) {
         const uint64_t pol_w = policy_evict_first();   // weights stream once
         const uint64_t pol_x = policy_evict_last();    // tokens are re-read by every weight tile
+        const int wr0 = n0 + (PAIR ? static_cast<int>(mt & 1) * C::kWRows : 0);  // first weight row loaded here
         for (int i = 0; i < nk; ++i) {
           const int st = i % C::kStages;
           const uint32_t ph = (i / C::kStages) & 1;
           if (!wait_bounded(bar_empty(st), ph ^ 1u, abort_flag, status, kStProducer, tmo)) break;
           const int kb = kb0 + i;
-          mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
           const uint32_t sa = base + C::kOffA + st * C::kABytes;
           const uint32_t sb = base + C::kOffB + st * C::kBBytes;
-          tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
-          if (p.w_packed) {
-            // packed: tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's full barrier
+            const uint32_t fb = dsmem_map(bar_full(st), leader_rank);
+            if (leader) mbar_arrive_expect_tx(bar_full(st), 2 * C::kStageBytes);
+            tma_load_2d_pair(sa, &tmap_x, fb, kb * kBlk, m0, pol_x);
+            if (p.w_packed) {
 #pragma unroll
-            for (int t = 0; t < (BN + 127) / 128; ++t) {
-              const int nb = (n0 >> 7) + t;
-              tma_load_2d(sb + t * 16384, &tmap_w, bar_full(st), 0, (nb * p.KB + kb) * kBlk + (n0 & 127), pol_w);
+              for (int t = 0; t < (C::kWRows + 127) / 128; ++t)
+                tma_load_2d_pair(sb + t * 16384, &tmap_w, fb, 0,
+                                 (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol_w);
+            } else {
+              tma_load_2d_pair(sb, &tmap_w, fb, kb * kBlk, wr0, pol_w);
             }
           } else {
-            tma_load_2d(sb, &tmap_w, bar_full(st), kb * kBlk, n0, pol_w);
+            mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+            tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
+            if (p.w_packed) {
+              // packed: tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128
+#pragma unroll
+              for (int t = 0; t < (C::kWRows + 127) / 128; ++t)
+                tma_load_2d(sb + t * 16384, &tmap_w, bar_full(st), 0,
+                            (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol_w);
+            } else {
+              tma_load_2d(sb, &tmap_w, bar_full(st), kb * kBlk, wr0, pol_w);
+            }
           }
           produced = i + 1;
         }
       }
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer --
-      if (lane == 0) {
-        constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, BN);
+      if (lane == 0 && leader) {
+        constexpr uint32_t idesc = idesc_e4m3_f32(PAIR ? 2 * kTileM : kTileM, BN);
         for (int i = 0; i < nk; ++i) {
           const int st = i % C::kStages;
           const uint32_t ph = (i / C::kStages) & 1;
@@ -225,11 +342,18 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           const uint32_t d = tmem_base + buf * BN;
           const uint64_t da = sw128_kmajor_desc(base + C::kOffA + st * C::kABytes);
           const uint64_t db = sw128_kmajor_desc(base + C::kOffB + st * C::kBBytes);
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int k = 0; k < kBlk / 32; ++k)  // K = 32 e4m3 elements = 32 bytes = 2 descriptor units
-            umma_f8(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
-          umma_commit(bar_empty(st));
-          umma_commit(bar_tfull(buf));
+            for (int k = 0; k < kBlk / 32; ++k) umma_f8_pair(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+            umma_commit_pair_mc(bar_empty(st), pair_mask);   // frees the stage in both CTAs
+            umma_commit_pair_mc(bar_tfull(buf), pair_mask);  // both CTAs' accumulators are ready
+          } else {
+#pragma unroll
+            for (int k = 0; k < kBlk / 32; ++k)  // K = 32 e4m3 elements = 32 bytes = 2 descriptor units
+              umma_f8(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+            umma_commit(bar_empty(st));
+            umma_commit(bar_tfull(buf));
+          }
         }
       }
     }
@@ -240,6 +364,8 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     const int h = (warp - kEpiWarp0) >> 2;        // column half
     const int col0 = h * C::kCpw;
     const int tok = q * 32 + lane;                // token row inside the tile
+    // where this warp reports a released TMEM buffer: the MMA issuer's CTA
+    const uint32_t tempty_base = PAIR ? dsmem_map(bar_tempty(0), leader_rank) : bar_tempty(0);
     if (q < quarters) {
       float acc[C::kCpw];
 #pragma unroll
@@ -249,7 +375,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       // private shared slots (one commit group per K block).
       const int et = (warp - kEpiWarp0) * 32 + lane;
       const bool has = tok < rows;
-      const float* xs_row = p.x_scale + static_cast<int64_t>(has ? m0 + tok : m0) * p.xs_sm;
+      const float* xs_row = p.x_scale + static_cast<int64_t>(has ? m0 + tok : 0) * p.xs_sm;  // row 0 exists
       const float* ws_row = p.w_scale + static_cast<int64_t>((n0 + col0) >> 7) * p.KB;
       const uint32_t raw_x = base + C::kOffRaw + et * 4;
       const uint32_t raw_w = base + C::kOffRawW + et * 4;
@@ -303,7 +429,12 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_tempty(buf));
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_remote(tempty_base + 8u * buf);
+          else
+            mbar_arrive(bar_tempty(buf));
+        }
       }
       cp_async_wait<0>();  // no copy may land after the CTA exits
       if (done && *abort_flag == 0) {
@@ -336,34 +467,60 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
 
   // ------------------------------------------------------------ teardown --
+  // The next launch may start its prologue now; it still waits for this whole
+  // grid to finish before reading anything (grid_dependency_wait).
+  grid_launch_dependents();
   tc_fence_before();
-  __syncthreads();  // every role has left its loop: the abort flag is final from here on
+  __syncthreads();  // every role of this CTA has left its loop
   tc_fence_after();
-  const bool ok = (*abort_flag == 0);
   if (warp == 0) {
     // Producer: if the pipeline was abandoned, wait (bounded, fresh deadline)
     // for the TMA copies it issued so none lands after the CTA has exited.
-    if (!ok && lane == 0) {
+    if (*abort_flag && lane == 0) {
       const int first = produced > C::kStages ? produced - C::kStages : 0;
       volatile int no_abort = 0;
-      for (int i = first; i < produced; ++i)
-        wait_bounded(bar_full(i % C::kStages), (i / C::kStages) & 1, &no_abort, status, kStDrain, tmo);
+      if (leader) {
+        for (int i = first; i < produced; ++i)
+          wait_bounded(bar_full(i % C::kStages), (i / C::kStages) & 1, &no_abort, status, kStDrain, tmo);
+      } else {
+        // a pair's second CTA signals its loads on the leader's barrier and
+        // cannot observe them: give them a bounded 50 us to land
+        const uint64_t t0 = global_timer_ns();
+        while (global_timer_ns() - t0 < 50000u) __nanosleep(1000);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
     // No MMA may still be writing TMEM when it is freed: commit arrives once
     // every earlier tcgen05.mma of this thread has completed.
-    if (lane == 0) {
-      umma_commit(bar_drain);
+    if (lane == 0 && leader) {
+      if constexpr (PAIR)
+        umma_commit_pair(bar_drain);
+      else
+        umma_commit(bar_drain);
       volatile int no_abort = 0;
       wait_bounded(bar_drain, 0, &no_abort, status, kStDrain, tmo);
     }
     __syncwarp();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if constexpr (PAIR) {
+    // the leader's MMAs have drained and the peer's loads were consumed (or
+    // drained): only now may either CTA free its TMEM, and neither exits
+    // while the other may still signal its barriers
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+  }
+  const bool ok = (*abort_flag == 0);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, C::kTmemCols);
   }
 
   if (S == 1) {
-    if (!ok) return;
+    if (!ok || rows <= 0) return;
     // 16-byte vectors of the staged bf16 tile along rows of Y
     const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffA);
     constexpr int kRowChunks = BN / 8;
@@ -375,48 +532,38 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     return;
   }
 
-  // Split-K: copy the staged fp32 partial to the workspace, publish it to the
-  // cluster (every CTA arrives, also after an abort, so no CTA of the cluster
-  // waits forever), then reduce a disjoint block of rows over the slices in
-  // fixed order.
-  const int64_t tile = static_cast<int64_t>(mt) * gridDim.x + nt;
-  constexpr int kRowF4 = BN / 4;
+  // Split-K.  Every CTA of the cluster arrives at every cluster barrier, also
+  // after an abort, so none waits forever; each then sums a disjoint block of
+  // rows over the slices in fixed order 0..S-1 (bitwise reproducible).
+  const int rows_v = rows > 0 ? rows : 0;
+  const int per = (rows_v + S - 1) / S;
+  const int r0 = s * per;
+  const int r1 = min(rows_v, r0 + per);
+  const int rank_step = PAIR ? 2 : 1;               // cluster rank of slice t: (mt & 1) + rank_step * t
+  const int rank0 = PAIR ? static_cast<int>(mt & 1) : 0;
+  if (p.partials == nullptr) {
+    // Partials stay in each CTA's shared staging tile; peers read them over
+    // distributed shared memory.  The second barrier keeps every CTA (and so
+    // its shared memory) alive until all peers have finished reading.
+    cluster_sync_all();
+    if (ok)
+      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1,
+                                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+    cluster_sync_all();
+    return;
+  }
+  // Caller-provided workspace: copy the staged partial there (L2), publish it
+  // with the cluster barrier, and reduce from global memory.
+  const int64_t tile = static_cast<int64_t>(mt) * (p.N / BN) + nt;
   if (ok) {
-    const float* stg = reinterpret_cast<const float*>(smem + C::kOffA);
-    float* part = p.partials + (tile * S + s) * kTileM * BN;
-    for (int c = threadIdx.x; c < rows * kRowF4; c += kThreads) {
-      const int r = c / kRowF4, c4 = c % kRowF4;
-      __stcg(reinterpret_cast<float4*>(part + r * BN + c4 * 4),
-             *reinterpret_cast<const float4*>(stg + r * C::kPitch32 + c4 * 4));
-    }
+    copy_partial<BN, C::kPitch32>(reinterpret_cast<const float*>(smem + C::kOffA), rows_v,
+                                  p.partials + (tile * S + s) * kTileM * BN);
     __threadfence();
   }
   cluster_sync_all();
   if (!ok) return;
-  const float* part0 = p.partials + tile * S * kTileM * BN;
-  const int per = (rows + S - 1) / S;
-  const int r0 = s * per;
-  const int r1 = min(rows, r0 + per);
-  const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
-  for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int r = r0 + it / kRowF4;
-    const int c4 = it % kRowF4;
-    const float* src = part0 + r * BN + c4 * 4;
-    float4 sum = __ldcg(reinterpret_cast<const float4*>(src));
-    for (int t = 1; t < S; ++t) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
-      sum.x += v.x;
-      sum.y += v.y;
-      sum.z += v.z;
-      sum.w += v.w;
-    }
-    __nv_bfloat162 lo = __floats2bfloat162_rn(sum.x, sum.y);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(sum.z, sum.w);
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-    pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(p.out + static_cast<int64_t>(m0 + r) * p.ldo + n0 + c4 * 4) = pk;
-  }
+  reduce_global<BN>(p.partials + tile * S * kTileM * BN, S, r0, r1,
+                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
 }
 
 // ------------------------------------------------------------------ prepack --
@@ -463,9 +610,9 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 constexpr int kMaxDevices = 64;
 
-constexpr int kVariants = 3;  // weight tiles 64, 128, 256
+constexpr int kVariants = 6;  // weight tiles 64, 128, 256 x (single CTA, CTA pair)
 
-static int variant(int bn) { return bn == 64 ? 0 : bn == 128 ? 1 : 2; }
+static int variant(int tm, int bn) { return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0); }
 
 struct DeviceInfo {
   bool init = false;
@@ -476,6 +623,16 @@ struct DeviceInfo {
 };
 
 static std::mutex g_mu;
+static thread_local char g_last_error[256] = "";
+
+// Records why a call failed (for fack_last_error) and returns `status`.
+static int fail(int status, const char* what, cudaError_t err = cudaSuccess) {
+  if (err != cudaSuccess)
+    snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
+  else
+    snprintf(g_last_error, sizeof(g_last_error), "%s", what);
+  return status;
+}
 static DeviceInfo g_dev[kMaxDevices];
 static EncodeTiledFn g_encode = nullptr;
 
@@ -516,60 +673,63 @@ struct KernelEntry {
   int smem;
 };
 
-template <int BN>
+template <int BN, bool PAIR>
 static KernelEntry entry() {
-  return {reinterpret_cast<const void*>(gemm_bs_kernel<BN>), Cfg<BN>::kSmemBytes};
+  return {reinterpret_cast<const void*>(gemm_bs_kernel<BN, PAIR>), Cfg<BN, PAIR>::kSmemBytes};
 }
 
-static const KernelEntry& kernel_for(int bn) {
-  static const KernelEntry table[kVariants] = {entry<64>(), entry<128>(), entry<256>()};
-  return table[variant(bn)];
+static const KernelEntry& kernel_for(int tm, int bn) {
+  static const KernelEntry table[kVariants] = {entry<64, false>(), entry<128, false>(), entry<256, false>(),
+                                               entry<64, true>(),  entry<128, true>(),  entry<256, true>()};
+  return table[variant(tm, bn)];
 }
 
-static int ensure_configured(DeviceInfo* d, int bn) {
-  const int v = variant(bn);
+static int ensure_configured(DeviceInfo* d, int tm, int bn) {
+  const int v = variant(tm, bn);
   std::lock_guard<std::mutex> lk(g_mu);
   if (!(d->configured & (1u << v))) {
-    const KernelEntry& k = kernel_for(bn);
+    const KernelEntry& k = kernel_for(tm, bn);
     // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
     // launch; with any other count setmaxnreg.inc could wait forever, so the
     // kernel is refused instead of launched.
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, k.fn) != cudaSuccess || fa.numRegs != kLaunchRegs ||
-        fa.maxThreadsPerBlock < kThreads)
-      return FACK_ERR_LAUNCH;
-    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) != cudaSuccess)
-      return FACK_ERR_LAUNCH;
+    cudaError_t e = cudaFuncGetAttributes(&fa, k.fn);
+    if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaFuncGetAttributes", e);
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+      return fail(FACK_ERR_LAUNCH, "kernel register count differs from the setmaxnreg budget; refusing to launch");
+    e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+    if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaFuncSetAttribute(max dynamic shared memory)", e);
     d->configured |= 1u << v;
   }
   return FACK_OK;
 }
 
-// How many clusters of `split` CTAs (or, for split 1, single CTAs) of the
-// weight-tile variant `bn` the device holds at once.  Clusters must fit inside
-// one GPC, so on B200 fewer than 148/split clusters of a size fit.
-static int co_resident(DeviceInfo* d, int bn, int split) {
-  const int v = variant(bn);
+// How many clusters of the (tm, bn) variant with `split` K slices the device
+// holds at once.  A cluster is (tm/128, 1, split) CTAs and must fit inside
+// one GPC, so on B200 fewer than 148/size clusters of a size fit.
+static int co_resident(DeviceInfo* d, int tm, int bn, int split) {
+  const int v = variant(tm, bn);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (d->clusters[v][split]) return d->clusters[v][split];
   }
-  if (ensure_configured(d, bn) != FACK_OK) return 0;
-  const KernelEntry& k = kernel_for(bn);
+  if (ensure_configured(d, tm, bn) != FACK_OK) return 0;
+  const KernelEntry& k = kernel_for(tm, bn);
+  const int cx = tm / kTileM;  // pairs along cluster x
   int n = 0;
-  if (split == 1) {
+  if (split == 1 && cx == 1) {
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kThreads, k.smem) != cudaSuccess) return 0;
     n = per_sm * d->sms;
   } else {
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(1, 1, split);
+    cfg.gridDim = dim3(cx, 1, split);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.x = cx;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = split;
     cfg.attrs = attr;
@@ -581,65 +741,107 @@ static int co_resident(DeviceInfo* d, int bn, int split) {
   return n;
 }
 
-// Plan (weight tile BN, split-K S): the stand-in for aiter's tuned
-// (M,N,K,cu_num) table.  Estimated time of a launch, in SM cycles:
-//   waves x K-steps per CTA x max(control floor, MMA, rescale)
-//   + for S > 1: fp32 partial write + re-read and the cluster barrier,
-// bounded below by the HBM time of the operands.  A wave is the number of
-// tiles the device holds at once (clusters of S CTAs must fit in one GPC).
-static double plan_cost(DeviceInfo* d, int M, int N, int K, int bn, int sp) {
+// Grid of a plan.  Single CTAs: x = weight tiles, y = 128-token tiles.  CTA
+// pairs: x = 128-token tiles (an even count; a pair's second CTA may hold no
+// valid token) so that the pair lies along the cluster's x dimension,
+// y = weight tiles.  z = K slices.
+static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, int* gz) {
+  if (tm == 256) {
+    *gx = 2 * ((M + 255) / 256);
+    *gy = N / bn;
+  } else {
+    *gx = N / bn;
+    *gy = (M + kTileM - 1) / kTileM;
+  }
+  *gz = sp;
+}
+
+// Plan (token tile tm = 128 | 256 for a CTA pair, weight tile bn, split-K sp):
+// the stand-in for aiter's tuned (M,N,K,cu_num) table.  Estimated launch time
+// in SM cycles: waves of co-resident clusters x K steps per CTA x the slowest
+// of {control floor, MMA, rescale, operand ingest at ~55 GB/s per SM}, plus
+// the split-K combine, bounded below by the HBM time of the operands.
+static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int sp) {
   const int KB = K / kBlk;
-  const int mtiles = (M + kTileM - 1) / kTileM;
-  const int tiles = mtiles * (N / bn);
-  const int slots = co_resident(d, bn, sp);
+  const int tiles = (N / bn) * ((M + tm - 1) / tm);
+  const int slots = co_resident(d, tm, bn, sp);
   if (slots <= 0) return 1e30;
   const int waves = (tiles + slots - 1) / slots;
   const int steps = (KB + sp - 1) / sp;
-  const int quarters = (M >= kTileM) ? 4 : (M + 31) / 32;
-  const double t_kb = fmax(fmax(450.0, 2.0 * bn), 0.45 * bn * quarters + 150.0);
+  const int m_cta = M < kTileM ? M : kTileM;                      // valid tokens of a full CTA tile
+  const int quarters = (m_cta + 31) / 32;
+  const double wrows = tm == 256 ? bn / 2.0 : bn;
+  const double ingest = (m_cta * 128.0 + wrows * 128.0) / 55e9 * 1.9e9;
+  const double t_kb = fmax(fmax(600.0, 2.0 * bn), fmax(0.45 * bn * quarters + 150.0, ingest));
   double cyc = static_cast<double>(waves) * steps * t_kb + 2500.0;
   if (sp > 1) cyc += 1500.0 + 2.0 * kTileM * bn * 4.0 / 96.0;
-  const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K * (N / bn);
-  const double hbm_cyc = bytes / 6.5e12 * 1.9e9;
-  return fmax(cyc, hbm_cyc);
+  const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K;
+  return fmax(cyc, bytes / 6.5e12 * 1.9e9);
 }
 
-// Weight tile for an explicitly requested split (no device query needed, so
-// the workspace size of an explicit split is a pure function of the shape):
-// the largest tile that still gives >= 120 CTAs, else the smallest.
-static int tile_for_split(int M, int N, int sp) {
-  const int mtiles = (M + kTileM - 1) / kTileM;
-  for (int bn : {256, 128})
-    if (N % bn == 0 && mtiles * (N / bn) * sp >= 120) return bn;
-  return 64;
+// Tiles for an explicitly requested split (no device query, so the workspace
+// size of an explicit split is a pure function of the shape): single-CTA
+// token tiles unless pairs are requested, then the largest weight tile that
+// still gives >= 120 CTAs, else the smallest.
+static void tiles_for_split(int M, int N, int sp, int tm_req, int bn_req, int* tm, int* bn) {
+  int t = tm_req ? tm_req : 128;
+  int b = bn_req;
+  if (!b) {
+    b = 64;
+    for (int c : {256, 128}) {
+      int gx, gy, gz;
+      if (N % c) continue;
+      plan_grid(M, N, t, c, sp, &gx, &gy, &gz);
+      if (gx * gy * gz >= 120) {
+        b = c;
+        break;
+      }
+    }
+  }
+  *tm = t;
+  *bn = b;
 }
 
-static int plan_auto(DeviceInfo* d, int M, int N, int K, int* bn_out, int* sp_out) {
+static size_t workspace_bytes_for(int M, int N, int tm, int bn, int split);
+
+// Best plan by plan_cost among those whose split-K workspace (when combined
+// through global memory) is at most ws_cap bytes.
+static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req, int* tm_out, int* bn_out,
+                     int* sp_out, size_t ws_cap = ~size_t(0)) {
   const int KB = K / kBlk;
   double best = 1e30;
-  int bb = 0, bs = 0;
-  for (int bn : {256, 128, 64}) {
-    if (N % bn) continue;
-    for (int sp = 1; sp <= kMaxSplit && sp <= KB; ++sp) {
-      if (sp > 1 && KB / sp < 2) break;
-      const double c = plan_cost(d, M, N, K, bn, sp);
-      if (c < best * 0.97) {  // prefer the larger tile / smaller split unless clearly faster
-        best = c;
-        bb = bn;
-        bs = sp;
+  int bt = 0, bb = 0, bs = 0;
+  // CTA pairs are chosen only on request for now: their cross-CTA handshakes
+  // currently cost more per K block than the weight bytes they save.
+  for (int tm : {128, 256}) {
+    if (tm_req ? tm != tm_req : tm != 128) continue;
+    for (int bn : {256, 128, 64}) {
+      if (N % bn || (bn_req && bn != bn_req)) continue;
+      for (int sp = 1; sp <= KB && sp * (tm / kTileM) <= kMaxSplit; ++sp) {
+        if (sp > 1 && KB / sp < 2) break;
+        if (workspace_bytes_for(M, N, tm, bn, sp) > ws_cap) continue;
+        const double c = plan_cost(d, M, N, K, tm, bn, sp);
+        if (c < best * 0.97) {  // prefer the earlier candidate unless clearly faster
+          best = c;
+          bt = tm;
+          bb = bn;
+          bs = sp;
+        }
       }
     }
   }
   if (!bb) return FACK_ERR_LAUNCH;
+  *tm_out = bt;
   *bn_out = bb;
   *sp_out = bs;
   return FACK_OK;
 }
 
-static size_t workspace_bytes_for(int M, int N, int bn, int split) {
+static size_t workspace_bytes_for(int M, int N, int tm, int bn, int split) {
   if (split <= 1) return 0;
-  const size_t tiles = static_cast<size_t>(N / bn) * ((M + kTileM - 1) / kTileM);
-  return tiles * split * kTileM * bn * sizeof(float);
+  int gx, gy, gz;
+  plan_grid(M, N, tm, bn, split, &gx, &gy, &gz);
+  return static_cast<size_t>(gx) * gy * split * kTileM * bn * sizeof(float);
 }
 
 static int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
@@ -655,29 +857,37 @@ static int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS ? FACK_OK : FACK_ERR_BAD_ALIGN;
 }
 
-static int launch(DeviceInfo* d, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int M,
-                  cudaStream_t stream) {
-  const int st = ensure_configured(d, bn);
+static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
+                  int M, cudaStream_t stream) {
+  const int st = ensure_configured(d, tm, bn);
   if (st != FACK_OK) return st;
-  const KernelEntry& k = kernel_for(bn);
+  const KernelEntry& k = kernel_for(tm, bn);
+  int gx, gy, gz;
+  plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(p.N / bn, (M + kTileM - 1) / kTileM, p.split);
+  cfg.gridDim = dim3(gx, gy, gz);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.attrs = attr;
   cfg.numAttrs = 0;
-  if (p.split > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = p.split;
-    cfg.numAttrs = 1;
+  // programmatic dependent launch: this kernel's prologue may overlap the
+  // previous kernel in the stream (see grid_dependency_wait in the kernel)
+  attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+  ++cfg.numAttrs;
+  if (p.split > 1 || tm == 256) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = tm / kTileM;  // CTA pairs lie along cluster x
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = p.split;
+    ++cfg.numAttrs;
   }
   void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tx), const_cast<Params*>(&p)};
-  if (cudaLaunchKernelExC(&cfg, k.fn, args) != cudaSuccess) return FACK_ERR_LAUNCH;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, k.fn, args);
+  if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaLaunchKernelExC", e);
   return FACK_OK;
 }
 
@@ -736,52 +946,45 @@ const char* fack_status_string(int status) {
 
 int fack_version(void) { return 100; }
 
-int fack_gemm_bs_plan(int M, int N, int K, int tile_n_request, int split_k_request, int* tile_n, int* split_k,
-                      size_t* workspace_bytes) {
+const char* fack_last_error(void) { return g_last_error; }
+
+int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_request, int split_k_request,
+                      int* tile_m, int* tile_n, int* split_k, size_t* workspace_bytes) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
-  if (!tile_n || !split_k) return FACK_ERR_BAD_ARG;
+  if (!tile_m || !tile_n || !split_k) return FACK_ERR_BAD_ARG;
   const int KB = K / kBlk;
   if (split_k_request < 0 || split_k_request > kMaxSplit || split_k_request > KB) return FACK_ERR_BAD_ARG;
+  if (tile_m_request != 0 && tile_m_request != 128 && tile_m_request != 256) return FACK_ERR_BAD_ARG;
   if (tile_n_request != 0 && tile_n_request != 64 && tile_n_request != 128 && tile_n_request != 256)
     return FACK_ERR_BAD_ARG;
   if (tile_n_request && N % tile_n_request) return FACK_ERR_BAD_ARG;
-  int bn = tile_n_request, sp = split_k_request;
-  if (sp && !bn) {
-    bn = tile_for_split(M, N, sp);
-  } else if (!sp) {
+  if (tile_m_request == 256 && split_k_request * 2 > kMaxSplit) return FACK_ERR_BAD_ARG;  // cluster of 2 x split
+  int tm = tile_m_request, bn = tile_n_request, sp = split_k_request;
+  if (sp) {
+    tiles_for_split(M, N, sp, tm, bn, &tm, &bn);
+  } else {
     DeviceInfo* d = nullptr;
     const int st = device_info(&d);
     if (st != FACK_OK) return st;
-    if (bn) {
-      double best = 1e30;
-      for (int c = 1; c <= kMaxSplit && c <= KB; ++c) {
-        if (c > 1 && KB / c < 2) break;
-        const double cost = plan_cost(d, M, N, K, bn, c);
-        if (cost < best * 0.97) {
-          best = cost;
-          sp = c;
-        }
-      }
-      if (!sp) return FACK_ERR_LAUNCH;
-    } else {
-      const int st2 = plan_auto(d, M, N, K, &bn, &sp);
-      if (st2 != FACK_OK) return st2;
-    }
+    const int st2 = plan_auto(d, M, N, K, tm, bn, &tm, &bn, &sp);
+    if (st2 != FACK_OK) return st2;
   }
+  *tile_m = tm;
   *tile_n = bn;
   *split_k = sp;
-  if (workspace_bytes) *workspace_bytes = workspace_bytes_for(M, N, bn, sp);
+  if (workspace_bytes) *workspace_bytes = workspace_bytes_for(M, N, tm, bn, sp);
   return FACK_OK;
 }
 
 int fack_gemm_bs_select(int M, int N, int K, int split_k_request, int* tile_n, int* split_k) {
-  return fack_gemm_bs_plan(M, N, K, 0, split_k_request, tile_n, split_k, nullptr);
+  int tm = 0;
+  return fack_gemm_bs_plan(M, N, K, 0, 0, split_k_request, &tm, tile_n, split_k, nullptr);
 }
 
 int fack_gemm_bs_workspace_size(int M, int N, int K, int split_k, size_t* bytes) {
   if (!bytes) return FACK_ERR_BAD_ARG;
-  int bn = 0, sp = 0;
-  return fack_gemm_bs_plan(M, N, K, 0, split_k, &bn, &sp, bytes);
+  int tm = 0, bn = 0, sp = 0;
+  return fack_gemm_bs_plan(M, N, K, 0, 0, split_k, &tm, &bn, &sp, bytes);
 }
 
 int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, int N, int K, void* wq_packed,
@@ -811,7 +1014,8 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, in
 
 int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
                     int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
-                    int N, int K, int tile_n, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
+                    int N, int K, int tile_m, int tile_n, int split_k, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
   if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
   if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
@@ -825,18 +1029,21 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != FACK_OK) return st;
-  int bn = 0, sp = 0;
+  int tm = 0, bn = 0, sp = 0;
   size_t need = 0;
-  st = fack_gemm_bs_plan(M, N, K, tile_n, split_k, &bn, &sp, &need);
+  st = fack_gemm_bs_plan(M, N, K, tile_m, tile_n, split_k, &tm, &bn, &sp, &need);
   if (st != FACK_OK) return st;
-  if (need && (!workspace || workspace_bytes < need || !aligned(workspace, 16))) return FACK_ERR_WS_TOO_SMALL;
+  const int wrows = tm == 256 ? bn / 2 : bn;  // weight rows one CTA loads
+  // A NULL workspace selects the distributed-shared-memory split-K reduction.
+  if (need && workspace && (workspace_bytes < need || !aligned(workspace, 16))) return FACK_ERR_WS_TOO_SMALL;
+  if (!workspace) workspace_bytes = 0;
 
   CUtensorMap tw, tx;
   if (wq_packed == FACK_W_PACKED)
-    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk, bn < kBlk ? bn : kBlk,
+    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk, wrows < kBlk ? wrows : kBlk,
                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);  // packed tiles are contiguous
   else
-    st = encode_2d(&tw, wq, K, N, K, kBlk, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_2d(&tw, wq, K, N, K, kBlk, wrows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
   st = encode_2d(&tx, xq, K, M, ldx, kBlk, kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
@@ -858,23 +1065,32 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
   p.timeout_ns = 2000000000ull;  // 2 s: far above any legitimate wait, short enough to report a lost arrival
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return launch(d, bn, tw, tx, p, M, s);
+  return launch(d, tm, bn, tw, tx, p, M, s);
 }
 
 int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
                  int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
                  int N, int K, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
   return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, 0,
-                         split_k, workspace, workspace_bytes, stream);
+                         0, split_k, workspace, workspace_bytes, stream);
 }
 
 int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
                          int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
                          int M, int N, int K, int split_k, void* stream) {
-  int bn = 0, sp = 0;
+  int tm = 0, bn = 0, sp = 0;
   size_t need = 0;
-  int st = fack_gemm_bs_plan(M, N, K, 0, split_k, &bn, &sp, &need);
+  int st = fack_gemm_bs_plan(M, N, K, 0, 0, split_k, &tm, &bn, &sp, &need);
   if (st != FACK_OK) return st;
+  if (need > kNoAllocScratchBytes && split_k == 0) {
+    // the library's own choice: take the best plan whose partials fit the buffer
+    DeviceInfo* d = nullptr;
+    st = device_info(&d);
+    if (st != FACK_OK) return st;
+    st = plan_auto(d, M, N, K, 0, 0, &tm, &bn, &sp, kNoAllocScratchBytes);
+    if (st != FACK_OK) return FACK_ERR_SCRATCH_LIMIT;
+    need = workspace_bytes_for(M, N, tm, bn, sp);
+  }
   if (need > kNoAllocScratchBytes) return FACK_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if (need) {
@@ -882,8 +1098,8 @@ int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_pac
     if (st != FACK_OK) return st;
   }
   // The same kernel and plan as fack_gemm_bs; only the workspace differs.
-  return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, bn,
-                         sp, scratch, need ? kNoAllocScratchBytes : 0, stream);
+  return fack_gemm_bs_ex(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, M, N, K, tm,
+                         bn, sp, scratch, need ? kNoAllocScratchBytes : 0, stream);
 }
 
 int fack_gather_interleave(const void* gathered, int g, int M, int n_shard, void* out, int64_t ldo, void* stream) {

@@ -32,9 +32,11 @@ Two layers:
 
 Every entry validates on the host and raises ``ValueError`` for a contract
 violation before launching, like the reference driver
-(client/aiter/hsa/gfx942/driver.py:11-12).  Calls allocate nothing except the
-split-K workspace, which is cached per (device, stream) and grown only outside
-CUDA-graph capture, so a warmed-up call is capturable.
+(client/aiter/hsa/gfx942/driver.py:11-12).  Calls allocate nothing: split-K
+slices are combined through the thread-block cluster's distributed shared
+memory (``reduce="global"`` instead uses a workspace cached per (device,
+stream), grown only outside CUDA-graph capture), so every call is
+capturable.
 """
 from __future__ import annotations
 
@@ -68,40 +70,43 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
-def kernel_name(tile_n: int, split_k: int) -> str:
-    return f"{KERNEL_PREFIX}_t128x{tile_n}_s{split_k}"
+def kernel_name(tile_m: int, tile_n: int, split_k: int) -> str:
+    return f"{KERNEL_PREFIX}_t{tile_m}x{tile_n}_s{split_k}"
 
 
 def parse_kernel_name(name) -> tuple:
-    """(tile_n, split_k) encoded in one of this library's kernel names, else (0, 0).
+    """(tile_m, tile_n, split_k) encoded in one of this library's kernel names,
+    else (0, 0, 0).
 
     The reviewed gfx942 symbols name AMD code objects and carry no tile that
     applies here, so they (and None / "") leave the choice to the library."""
     if not name or name in AITER_SYMBOLS:
-        return 0, 0
-    m = re.fullmatch(KERNEL_PREFIX + r"_t128x(64|128|256)_s([1-8])", str(name))
-    if not m:
+        return 0, 0, 0
+    m = re.fullmatch(KERNEL_PREFIX + r"_t(128|256)x(64|128|256)_s([1-8])", str(name))
+    if not m or (m.group(1) == "256" and int(m.group(3)) > 4):
         raise ValueError(f"unknown blockscale kernel {name!r}")
-    return int(m.group(1)), int(m.group(2))
+    return int(m.group(1)), int(m.group(2)), int(m.group(3))
 
 
-def plan(M: int, N: int, K: int, tile_n: int = 0, split_k: int = 0) -> tuple:
-    """(tile_n, split_k, workspace_bytes) the library uses; 0 = library choice."""
+def plan(M: int, N: int, K: int, tile_m: int = 0, tile_n: int = 0, split_k: int = 0) -> tuple:
+    """(tile_m, tile_n, split_k, workspace_bytes) the library uses; 0 = library choice."""
     lib = _lib.load()
-    tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
-    _lib.check(lib.fack_gemm_bs_plan(int(M), int(N), int(K), int(tile_n), int(split_k), ctypes.byref(tn),
-                                     ctypes.byref(sk), ctypes.byref(nb)), "fack_gemm_bs_plan")
-    return tn.value, sk.value, nb.value
+    tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    _lib.check(lib.fack_gemm_bs_plan(int(M), int(N), int(K), int(tile_m), int(tile_n), int(split_k),
+                                     ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk), ctypes.byref(nb)),
+               "fack_gemm_bs_plan")
+    return tm.value, tn.value, sk.value, nb.value
 
 
 def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     """Kernel and split-K this library uses for (M, N, K) on the current device."""
-    tn, sk, _ = plan(M, N, K, 0, split_k)
-    return {"libtype": "asm", "kernelName": kernel_name(tn, sk), "splitK": sk, "tile_m": 128, "tile_n": tn}
+    tm, tn, sk, _ = plan(M, N, K, 0, 0, split_k)
+    return {"libtype": "asm", "kernelName": kernel_name(tm, tn, sk), "splitK": sk, "tile_m": tm, "tile_n": tn}
 
 
-def workspace_size(M: int, N: int, K: int, split_k: int = 0, tile_n: int = 0) -> int:
-    return plan(M, N, K, tile_n, split_k)[2]
+def workspace_size(M: int, N: int, K: int, split_k: int = 0, tile_m: int = 0, tile_n: int = 0) -> int:
+    """Bytes of split-K workspace for the plan (only needed with workspace="global")."""
+    return plan(M, N, K, tile_m, tile_n, split_k)[3]
 
 
 def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
@@ -140,24 +145,29 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
         raise ValueError("all tensors must be on one device")
 
 
-def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_n=0):
+def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m=0, tile_n=0,
+            reduce="dsmem"):
+    """reduce = "dsmem": split-K slices combine through the cluster's shared
+    memory (no workspace, nothing allocated); "global": through a cached
+    workspace in global memory."""
     M, K = xq.shape
     N = wq.shape[0]
     dev = xq.device
     lib = _lib.load()
     with torch.cuda.device(dev):
-        tn, sk, need = plan(M, N, K, tile_n, split_k)
-        ws = _workspace(dev, need)
+        tm, tn, sk, need = plan(M, N, K, tile_m, tile_n, split_k)
+        ws = _workspace(dev, need) if reduce == "global" else None
         st = lib.fack_gemm_bs_ex(
             xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
             x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0),
-            M, N, K, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
+            M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
     _lib.check(st, "fack_gemm_bs_ex")
     return out
 
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
-                    out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0) -> torch.Tensor:
+                    out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0, tile_m: int = 0,
+                    reduce: str = "dsmem") -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
@@ -177,7 +187,10 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
         sk = max(sk, 1)
     if M == 1:
         sm = max(sm, 1)
-    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_n)
+    if reduce not in ("dsmem", "global"):
+        raise ValueError("reduce must be 'dsmem' or 'global'")
+    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_m,
+                   tile_n, reduce)
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):
@@ -198,14 +211,15 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     (client/aiter/hsa/gfx942/dispatch_driver.py:66-67); ``zero_bias_buf`` is
     accepted and unused.  ``kernelName`` may be None, one of the reviewed
     gfx942 symbols (library choice of tile) or one of this library's names
-    ``fack_bs_sm100_t128x{64|128|256}_s{1..8}``, which fixes the weight tile
-    (and the split, unless ``splitK`` is given); ``splitK`` None/0 otherwise
-    lets the library choose.  ``bpreshuffle=True`` requires ``b`` from
+    ``fack_bs_sm100_t{128|256}x{64|128|256}_s{S}`` (token tile 256 = a CTA
+    pair, S <= 4 then; else S <= 8), which fixes the tiles (and the split,
+    unless ``splitK`` is given); ``splitK`` None/0 otherwise lets the library
+    choose.  ``bpreshuffle=True`` requires ``b`` from
     :func:`shuffle_weight`.
     """
     if bias is not None:
         raise ValueError("the blockscale operator takes no bias")
-    tile_n, name_split = parse_kernel_name(kernelName)
+    tile_m, tile_n, name_split = parse_kernel_name(kernelName)
     shuffled = bool(getattr(b, "is_shuffled", False))
     if bool(bpreshuffle) != shuffled:
         raise ValueError("bpreshuffle={} but the weight {} a shuffle_weight() output".format(
@@ -217,7 +231,7 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     _check_common(a, b, w_scale, out, M, N, K)
     sm, sk = _aiter_xscale_strides(x_scale, M, K // BLOCK)
     split = name_split if splitK is None else int(splitK)
-    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_n)
+    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_m, tile_n)
 
 
 def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bfloat16):

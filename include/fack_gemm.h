@@ -59,16 +59,24 @@ const char* fack_status_string(int status);
 /* Library ABI version: 100 * major + minor. */
 int fack_version(void);
 
+/* Detail of the last failure on the calling thread (CUDA error name and
+ * text where one was involved); empty if none.  Static per-thread storage. */
+const char* fack_last_error(void);
+
 /*
- * Full plan: weight-tile width (64, 128 or 256; 0 = library choice) and split-K
- * (1..8; 0 = library choice) for an (M,N,K) problem, with the workspace bytes
- * fack_gemm_bs_ex needs for that plan (0 for a single K slice).  A library
- * choice of either value queries the current device (cluster occupancy); a
- * fully explicit request does not.  Plays the role of aiter's per-shape
+ * Full plan for an (M,N,K) problem: the token tile (128 = one CTA per tile;
+ * 256 = a pair of CTAs sharing each tensor-core MMA through a 2-SM cluster,
+ * each loading half of the weight rows), the weight-tile width (64, 128 or
+ * 256), split-K (1..8; 2 x split <= 8 for pairs) -- 0 for any of them = the
+ * library's choice -- and the workspace bytes fack_gemm_bs_ex needs for that
+ * plan when the caller supplies a workspace (0 for a single K slice).  A
+ * library choice of split-K queries the current device (cluster occupancy); an
+ * explicit split does not.  Plays the role of aiter's per-shape
  * kernelName/splitK selection (client/aiter/dispatch.py:142-150).
  */
-int fack_gemm_bs_plan(int M, int N, int K, int tile_n_request, int split_k_request,
-                      int* tile_n, int* split_k, size_t* workspace_bytes);
+int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_request,
+                      int split_k_request, int* tile_m, int* tile_n, int* split_k,
+                      size_t* workspace_bytes);
 
 /*
  * Tile / split-K plan the library uses for an (M,N,K) problem.  Every CTA
@@ -124,7 +132,8 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale,
  *             every element of the MxN block is written exactly once
  *   split_k   0 = library choice, else 1..8 (and <= K/128)
  *   workspace fp32 partials for split_k > 1, at least
- *             fack_gemm_bs_workspace_size() bytes, 16-byte aligned
+ *             fack_gemm_bs_workspace_size() bytes, 16-byte aligned; NULL
+ *             combines the K slices through distributed shared memory
  *
  * The split-K reduction is deterministic: slices are summed in a fixed order,
  * so repeated calls give bitwise-identical outputs.
@@ -136,14 +145,18 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                  void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * fack_gemm_bs with an explicit weight-tile width tile_n (0 = library choice),
- * the counterpart of aiter selecting one tile kernel by kernelName
+ * fack_gemm_bs with an explicit plan (tile_m, tile_n, split_k; 0 = library
+ * choice), the counterpart of aiter selecting one tile kernel by kernelName
  * (client/aiter/hsa/gfx942/driver.py:26-29 passes kernelName=symbol).
+ * For split_k > 1 the K slices of a tile are combined either through the
+ * caller's workspace (when `workspace` is not NULL; at least the plan's
+ * workspace bytes) or, with workspace = NULL, through the distributed shared
+ * memory of the tile's thread-block cluster (no global memory).
  */
 int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                     const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,
                     const float* w_scale, void* out, int64_t ldo,
-                    int M, int N, int K, int tile_n, int split_k,
+                    int M, int N, int K, int tile_m, int tile_n, int split_k,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
@@ -155,10 +168,11 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
  * reference (aiter's launcher allocates its own buffers).
  *
  * The split-K partial sums go to one 16 MiB buffer compiled into this library
- * (every GPU that loads the library keeps it until the process exits).
- * Problems whose plan needs more return FACK_ERR_SCRATCH_LIMIT before
- * anything is launched; a smaller split_k, or fack_gemm_bs with your own
- * workspace, avoids that.  Nothing in the buffer has to start at zero: each
+ * (every GPU that loads the library keeps it until the process exits).  With
+ * split_k = 0 the library picks its best plan whose partials fit the buffer;
+ * an explicit split_k whose partials do not fit returns FACK_ERR_SCRATCH_LIMIT
+ * before anything is launched (a smaller split_k, or fack_gemm_bs with your
+ * own workspace, avoids that).  Nothing in the buffer has to start at zero: each
  * call writes every partial it later reads.
  *
  * The buffer is shared by all calls on a device and keeps the last call's

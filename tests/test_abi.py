@@ -52,24 +52,37 @@ def test_bad_shapes_rejected(m, n, k):
 
 def test_explicit_split_plan_and_workspace_without_device():
     lib = _lib.load()
-    tn, sk = ctypes.c_int(), ctypes.c_int()
-    # 2 token tiles x 12 weight tiles of 256 x 6 slices = 144 CTAs -> 256-row weight tiles
-    assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tn), ctypes.byref(sk)) == 0
-    assert (tn.value, sk.value) == (256, 6)
-    # one token tile x 12 tiles = too few CTAs for 256 or 128 at split 1 -> 64-row tiles
-    assert lib.fack_gemm_bs_select(1, 3072, 7168, 1, ctypes.byref(tn), ctypes.byref(sk)) == 0
-    assert tn.value == 64
+    tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+
+    def plan(M, N, K, m=0, n=0, s=0):
+        st = lib.fack_gemm_bs_plan(M, N, K, m, n, s, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
+                                   ctypes.byref(nb))
+        return st, tm.value, tn.value, sk.value, nb.value
+
+    # requested pairs, split 4: 12 x 2 x 4 = 96 CTAs < 120 -> 128-wide weight tiles
+    assert plan(256, 3072, 7168, m=256, s=4)[:4] == (0, 256, 128, 4)
+    # 256 tokens, split 6: 12 x 2 x 6 = 144 CTAs with single-CTA 256-wide tiles
+    assert plan(256, 3072, 7168, s=6)[:4] == (0, 128, 256, 6)
+    # one token: single-CTA tiles; 12 CTAs at 256 -> smallest weight tile
+    assert plan(1, 3072, 7168, s=1)[1:3] == (128, 64)
     # N = 384 is not a multiple of 256
-    assert lib.fack_gemm_bs_select(300, 384, 7168, 8, ctypes.byref(tn), ctypes.byref(sk)) == 0
-    assert tn.value in (64, 128)
-    nb = ctypes.c_size_t()
-    assert lib.fack_gemm_bs_workspace_size(256, 3072, 7168, 6, ctypes.byref(nb)) == 0
-    assert nb.value == (2 * 12) * 6 * 128 * 256 * 4
-    assert lib.fack_gemm_bs_workspace_size(256, 3072, 7168, 1, ctypes.byref(nb)) == 0
-    assert nb.value == 0
-    # split beyond the cluster limit or beyond K/128 is refused
-    assert lib.fack_gemm_bs_select(256, 3072, 7168, 9, ctypes.byref(tn), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
-    assert lib.fack_gemm_bs_select(256, 3072, 256, 3, ctypes.byref(tn), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
+    assert plan(300, 384, 7168, s=8)[2] in (64, 128)
+    # workspace = tiles x split x 128 x tile_n x 4
+    st, m, n, s, ws = plan(256, 3072, 7168, m=128, n=256, s=6)
+    assert st == 0 and ws == (12 * 2) * 6 * 128 * 256 * 4
+    st, m, n, s, ws = plan(200, 3072, 7168, m=256, n=256, s=2)
+    assert st == 0 and ws == (12 * 2) * 2 * 128 * 256 * 4   # a pair: two 128-token tiles
+    assert plan(256, 3072, 7168, m=128, n=256, s=1)[4] == 0
+    assert lib.fack_gemm_bs_workspace_size(256, 3072, 7168, 1, ctypes.byref(nb)) == 0 and nb.value == 0
+    # refused: split beyond the cluster limit, beyond K/128, pairs with split > 4, odd tiles
+    assert plan(256, 3072, 7168, s=9)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(256, 3072, 256, s=3)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(256, 3072, 7168, m=256, s=5)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(256, 3072, 7168, m=64, s=1)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(256, 384, 7168, n=256, s=1)[0] == _lib.FACK_ERR_BAD_ARG
+    tn2, sk2 = ctypes.c_int(), ctypes.c_int()
+    assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tn2), ctypes.byref(sk2)) == 0
+    assert (tn2.value, sk2.value) == (256, 6)
 
 
 def test_pointer_and_stride_checks_before_device():

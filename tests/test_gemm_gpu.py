@@ -60,15 +60,16 @@ def test_golden_every_tile_and_split(cuda_device, name, packed):
     tile kernels) at every split-K the shape allows."""
     g = golden_on(name, cuda_device)
     b = fb.shuffle_weight(g["b"]) if packed else g["b"]
-    for tile in (64, 128, 256):
-        if g["n"] % tile:
-            continue
-        for split in range(1, min(8, g["k"] // 128) + 1):
-            out = poisoned(g["m"], g["n"], cuda_device)
-            fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=split,
-                                                    kernelName=f"fack_bs_sm100_t128x{tile}_s{split}",
-                                                    bpreshuffle=packed)
-            assert_close(out, g["reference"], f"{name} tile={tile} split={split} packed={packed}")
+    for tile_m in (128, 256):                      # 256 = a CTA pair sharing each MMA
+        for tile in (64, 128, 256):
+            if g["n"] % tile:
+                continue
+            for split in range(1, min(8 if tile_m == 128 else 4, g["k"] // 128) + 1):
+                out = poisoned(g["m"], g["n"], cuda_device)
+                fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=split,
+                                                        kernelName=f"fack_bs_sm100_t{tile_m}x{tile}_s{split}",
+                                                        bpreshuffle=packed)
+                assert_close(out, g["reference"], f"{name} tile={tile_m}x{tile} split={split} packed={packed}")
 
 
 @pytest.mark.parametrize("name", golden_names())
@@ -79,6 +80,11 @@ def test_golden_public_dispatch_and_native_layout(cuda_device, name):
     assert_close(y, g["reference"], name + " public")
     y2 = fb.gemm_blockscale(g["a"], g["b"], g["sa"], g["sb"])  # logical row-major x_scale
     assert_close(y2, g["reference"], name + " native")
+    if g["k"] >= 256:  # split-K combined through a global workspace instead of cluster shared memory
+        y3 = fb.gemm_blockscale(g["a"], g["b"], g["sa"], g["sb"], split_k=2, reduce="global")
+        assert_close(y3, g["reference"], name + " global reduce")
+        y4 = fb.gemm_blockscale(g["a"], g["b"], g["sa"], g["sb"], split_k=2, reduce="dsmem")
+        assert torch.equal(y3.view(torch.int16), y4.view(torch.int16))
     cfg = fb.get_config(g["m"], g["n"], g["k"])
     assert cfg["kernelName"].startswith("fack_bs_sm100_t") and cfg["splitK"] >= 1
 

@@ -55,13 +55,15 @@ def test_public_entry_rejects_non_bf16_output():
 
 
 def test_kernel_names_are_stable():
-    assert ops.kernel_name(256, 6) == "fack_bs_sm100_t128x256_s6"
+    assert ops.kernel_name(128, 256, 6) == "fack_bs_sm100_t128x256_s6"
 
 
 def test_kernel_name_round_trip():
-    assert ops.parse_kernel_name(ops.kernel_name(128, 3)) == (128, 3)
-    assert ops.parse_kernel_name(None) == (0, 0)
-    assert ops.parse_kernel_name("_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_96x128E") == (0, 0)
-    for bad in ("fack_bs_sm100_t128x96_s2", "fack_bs_sm100_t128x128_s9", "fack_bs_sm100_t256x128_s6"):
+    assert ops.parse_kernel_name(ops.kernel_name(128, 128, 3)) == (128, 128, 3)
+    assert ops.parse_kernel_name(ops.kernel_name(256, 64, 4)) == (256, 64, 4)
+    assert ops.parse_kernel_name(None) == (0, 0, 0)
+    assert ops.parse_kernel_name("_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_96x128E") == (0, 0, 0)
+    for bad in ("fack_bs_sm100_t128x96_s2", "fack_bs_sm100_t128x128_s9", "fack_bs_sm100_t256x128_s6",
+                "fack_bs_sm100_t64x128_s1"):
         with pytest.raises(ValueError):
             ops.parse_kernel_name(bad)

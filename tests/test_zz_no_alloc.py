@@ -40,8 +40,9 @@ def _args(xq, xs, wq, ws, out):
 def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
     lib = _lib.load()
     M, N, K = 256, 3072, 7168   # the decode shape: the library's plan splits K, so the scratch is used
-    tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
-    assert lib.fack_gemm_bs_plan(M, N, K, 0, 0, ctypes.byref(tn), ctypes.byref(sk), ctypes.byref(nb)) == 0
+    tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    assert lib.fack_gemm_bs_plan(M, N, K, 0, 0, 0, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
+                                 ctypes.byref(nb)) == 0
     assert sk.value > 1 and 0 < nb.value <= SCRATCH_BYTES
 
     xq, xs, wq, ws = data.make_inputs(data.Workload("noalloc", M, N, K), seed=17, device=cuda_device)
@@ -68,8 +69,9 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
 def test_noalloc_refuses_problems_beyond_its_scratch(cuda_device):
     lib = _lib.load()
     M, N, K = 8192, 7168, 16384  # split 8 would need ~1.9 GB of partials
-    tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
-    assert lib.fack_gemm_bs_plan(M, N, K, 0, 8, ctypes.byref(tn), ctypes.byref(sk), ctypes.byref(nb)) == 0
+    tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    assert lib.fack_gemm_bs_plan(M, N, K, 0, 0, 8, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
+                                 ctypes.byref(nb)) == 0
     assert nb.value > SCRATCH_BYTES
     fake = 1 << 20  # never dereferenced: the size check comes first
     st = lib.fack_gemm_bs_noalloc(fake, K, fake, 0, fake, K // 128, 1, fake, fake, N, M, N, K, 8, _stream())
