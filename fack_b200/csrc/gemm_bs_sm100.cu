@@ -43,6 +43,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/fack_gemm.h"
 #include "sm100_ptx.cuh"
@@ -56,6 +57,7 @@ constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..1
 constexpr int kEpiWarps = 8;
 constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
 constexpr int kMaxSplit = 8;       // portable cluster size
+constexpr int kGroupM = 16;        // token-tile band of the grouped launch order
 constexpr int kSmemBudget = 196608;
 // Register split (setmaxnreg).  The kernel is launched with kLaunchRegs per
 // thread (ptxas' cap for 384 threads, 3 warps per scheduler); warpgroup 0
@@ -129,25 +131,47 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float4& v
 
 // Split-K reduction over distributed shared memory: rows [r0, r1) of the
 // tile, summed over the S cluster CTAs' staged fp32 partials in rank order.
-// Kept out of line so its registers are allocated apart from the rescale loop.
-template <int BN, int PITCH>
-__device__ __noinline__ void reduce_dsmem(uint32_t stg, int S, int rank0, int rank_step, int r0, int r1,
+// A remote shared-memory load costs several hundred cycles, so each thread
+// first issues the loads of U items x S slices (<= 24 x 16 B in flight) and
+// only then adds them, slice by slice in fixed order.  Kept out of line so
+// its registers are allocated apart from the rescale loop; it runs after the
+// register split has been undone (every warp at the launch allocation).
+template <int BN, int PITCH, int S>
+__device__ __noinline__ void reduce_dsmem(uint32_t stg, int rank0, int rank_step, int r0, int r1,
                                           __nv_bfloat16* out, int64_t ldo) {
   constexpr int kRowF4 = BN / 4;
+  constexpr int U = (24 / S) > 1 ? 24 / S : 1;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
-  for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int r = r0 + it / kRowF4;
-    const int c4 = it % kRowF4;
-    const uint32_t addr = stg + static_cast<uint32_t>((r * PITCH + c4 * 4) * 4);
-    float4 sum = dsmem_ld4(dsmem_map(addr, rank0));
-    for (int t = 1; t < S; ++t) {
-      const float4 v = dsmem_ld4(dsmem_map(addr, rank0 + t * rank_step));
-      sum.x += v.x;
-      sum.y += v.y;
-      sum.z += v.z;
-      sum.w += v.w;
+  uint32_t peer[S];
+#pragma unroll
+  for (int t = 0; t < S; ++t) peer[t] = dsmem_map(stg, rank0 + t * rank_step);
+  for (int it0 = threadIdx.x; it0 < items; it0 += U * kThreads) {
+    float4 v[U][S];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + u * kThreads;
+      const int r = r0 + it / kRowF4;
+      const uint32_t off = static_cast<uint32_t>((r * PITCH + (it % kRowF4) * 4) * 4);
+      if (it < items) {
+#pragma unroll
+        for (int t = 0; t < S; ++t) v[u][t] = dsmem_ld4(peer[t] + off);
+      }
     }
-    store_bf16x4(out + r * ldo + c4 * 4, sum);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + u * kThreads;
+      if (it < items) {
+        float4 sum = v[u][0];
+#pragma unroll
+        for (int t = 1; t < S; ++t) {
+          sum.x += v[u][t].x;
+          sum.y += v[u][t].y;
+          sum.z += v[u][t].z;
+          sum.w += v[u][t].w;
+        }
+        store_bf16x4(out + (r0 + it / kRowF4) * ldo + (it % kRowF4) * 4, sum);
+      }
+    }
   }
 }
 
@@ -162,25 +186,54 @@ __device__ __noinline__ void copy_partial(const float* stg, int rows, float* par
   }
 }
 
-// Split-K reduction from the workspace: rows [r0, r1), slices in order.
-template <int BN>
-__device__ __noinline__ void reduce_global(const float* part0, int S, int r0, int r1, __nv_bfloat16* out,
-                                           int64_t ldo) {
+// Split-K reduction from the workspace: rows [r0, r1), slices in order, with
+// the loads of U items x S slices in flight per thread (as reduce_dsmem).
+template <int BN, int S>
+__device__ __noinline__ void reduce_global(const float* part0, int r0, int r1, __nv_bfloat16* out, int64_t ldo) {
   constexpr int kRowF4 = BN / 4;
+  constexpr int U = (24 / S) > 1 ? 24 / S : 1;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
-  for (int it = threadIdx.x; it < items; it += kThreads) {
-    const int r = r0 + it / kRowF4;
-    const int c4 = it % kRowF4;
-    const float* src = part0 + r * BN + c4 * 4;
-    float4 sum = __ldcg(reinterpret_cast<const float4*>(src));
-    for (int t = 1; t < S; ++t) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
-      sum.x += v.x;
-      sum.y += v.y;
-      sum.z += v.z;
-      sum.w += v.w;
+  for (int it0 = threadIdx.x; it0 < items; it0 += U * kThreads) {
+    float4 v[U][S];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + u * kThreads;
+      const float* src = part0 + (r0 + it / kRowF4) * BN + (it % kRowF4) * 4;
+      if (it < items) {
+#pragma unroll
+        for (int t = 0; t < S; ++t)
+          v[u][t] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
+      }
     }
-    store_bf16x4(out + r * ldo + c4 * 4, sum);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + u * kThreads;
+      if (it < items) {
+        float4 sum = v[u][0];
+#pragma unroll
+        for (int t = 1; t < S; ++t) {
+          sum.x += v[u][t].x;
+          sum.y += v[u][t].y;
+          sum.z += v[u][t].z;
+          sum.w += v[u][t].w;
+        }
+        store_bf16x4(out + (r0 + it / kRowF4) * ldo + (it % kRowF4) * 4, sum);
+      }
+    }
+  }
+}
+
+// Run body<S>() for the runtime slice count 2..kMaxSplit.
+template <typename F>
+__device__ __forceinline__ void with_split(int S, F&& body) {
+  switch (S) {
+    case 2: body(std::integral_constant<int, 2>{}); break;
+    case 3: body(std::integral_constant<int, 3>{}); break;
+    case 4: body(std::integral_constant<int, 4>{}); break;
+    case 5: body(std::integral_constant<int, 5>{}); break;
+    case 6: body(std::integral_constant<int, 6>{}); break;
+    case 7: body(std::integral_constant<int, 7>{}); break;
+    default: body(std::integral_constant<int, 8>{}); break;
   }
 }
 
@@ -205,9 +258,26 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
   // grid: single CTAs (x = weight tile, y = token tile); pairs (x = token
   // tile, so that the pair lies along the cluster's x dimension, y = weight
-  // tile); z = K slice
-  const int nt = PAIR ? blockIdx.y : blockIdx.x;   // weight tile (BN output columns)
-  const int mt = PAIR ? blockIdx.x : blockIdx.y;   // token tile (128 output rows)
+  // tile); z = K slice.  The launch order is remapped (grouped rasterization):
+  // within a K slice consecutive CTAs walk the token tiles of a band of
+  // kGroupM tiles before moving to the next weight tile, so the CTAs resident
+  // at one time share both operands in L2 instead of streaming all weights
+  // once per row of token tiles.
+  int mt, nt;
+  {
+    const int unit = PAIR ? 2 : 1;                               // CTAs per token-tile slot
+    const int m_slots = PAIR ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.y);
+    const int n_tiles = PAIR ? static_cast<int>(gridDim.y) : static_cast<int>(gridDim.x);
+    const int lin = PAIR ? static_cast<int>(blockIdx.x) / 2 + static_cast<int>(blockIdx.y) * m_slots
+                         : static_cast<int>(blockIdx.x) + static_cast<int>(blockIdx.y) * n_tiles;
+    const int per_group = kGroupM * n_tiles;
+    const int g = lin / per_group;
+    const int first = g * kGroupM;
+    const int gm = min(kGroupM, m_slots - first);
+    const int r = lin - g * per_group;
+    nt = r / gm;
+    mt = (first + r % gm) * unit + (PAIR ? static_cast<int>(blockIdx.x & 1) : 0);
+  }
   const int s = blockIdx.z;                        // K slice
   const int S = p.split;
   const int m0 = mt * kTileM;
@@ -470,6 +540,13 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // The next launch may start its prologue now; it still waits for this whole
   // grid to finish before reading anything (grid_dependency_wait).
   grid_launch_dependents();
+  // Undo the register split: the rescale warpgroups give back what they took
+  // before the control warpgroup reclaims it, so the teardown (drain, staged
+  // copy-out, split-K reduction) runs with the launch allocation in every warp.
+  if (warp >= kEpiWarp0)
+    regs_dec<kLaunchRegs>();
+  else
+    regs_inc<kLaunchRegs>();
   tc_fence_before();
   __syncthreads();  // every role of this CTA has left its loop
   tc_fence_after();
@@ -547,8 +624,10 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // its shared memory) alive until all peers have finished reading.
     cluster_sync_all();
     if (ok)
-      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1,
-                                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+      with_split(S, [&](auto sc) {
+        reduce_dsmem<BN, C::kPitch32, decltype(sc)::value>(base + C::kOffA, rank0, rank_step, r0, r1,
+                                                          p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+      });
     cluster_sync_all();
     return;
   }
@@ -562,8 +641,10 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   cluster_sync_all();
   if (!ok) return;
-  reduce_global<BN>(p.partials + tile * S * kTileM * BN, S, r0, r1,
-                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+  with_split(S, [&](auto sc) {
+    reduce_global<BN, decltype(sc)::value>(p.partials + tile * S * kTileM * BN, r0, r1,
+                                           p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+  });
 }
 
 // ------------------------------------------------------------------ prepack --
@@ -758,23 +839,32 @@ static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, in
 
 // Plan (token tile tm = 128 | 256 for a CTA pair, weight tile bn, split-K sp):
 // the stand-in for aiter's tuned (M,N,K,cu_num) table.  Estimated launch time
-// in SM cycles: waves of co-resident clusters x K steps per CTA x the slowest
-// of {control floor, MMA, rescale, operand ingest at ~55 GB/s per SM}, plus
-// the split-K combine, bounded below by the HBM time of the operands.
+// in SM cycles from per-SM rates measured on B200:
+//  * a K block costs the slowest of: operand ingest (TMA fill into shared
+//    memory, ~44 B/clk sustained per SM), the MMA (2*bn cycles for 128 rows),
+//    and the MMA -> rescale -> TMEM-release round trip, which 512 TMEM
+//    columns cannot hide at full MMA rate (~880 / 550 / 500 cycles for
+//    bn = 256 / 128 / 64);
+//  * per CTA ~4000 cycles of prologue, first-load latency and exit;
+//  * output: bf16 tile stores at ~24 B/clk (the SM's store path), or for
+//    split-K the exchange of (S-1)/S of the fp32 partial tile at ~18 B/clk
+//    plus two cluster barriers;
+// times the number of waves of co-resident clusters, bounded below by the HBM
+// time of the operands.
 static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int sp) {
   const int KB = K / kBlk;
-  const int tiles = (N / bn) * ((M + tm - 1) / tm);
-  const int slots = co_resident(d, tm, bn, sp);
+  const int tiles = (N / bn) * ((M + tm - 1) / tm) * (tm / kTileM);   // CTAs per K slice
+  const int slots = co_resident(d, tm, bn, sp) * (tm / kTileM);       // CTAs per K slice resident at once
   if (slots <= 0) return 1e30;
   const int waves = (tiles + slots - 1) / slots;
   const int steps = (KB + sp - 1) / sp;
-  const int m_cta = M < kTileM ? M : kTileM;                      // valid tokens of a full CTA tile
-  const int quarters = (m_cta + 31) / 32;
+  const int rows = M < kTileM ? M : kTileM;                          // valid tokens of a full CTA tile
   const double wrows = tm == 256 ? bn / 2.0 : bn;
-  const double ingest = (m_cta * 128.0 + wrows * 128.0) / 55e9 * 1.9e9;
-  const double t_kb = fmax(fmax(600.0, 2.0 * bn), fmax(0.45 * bn * quarters + 150.0, ingest));
-  double cyc = static_cast<double>(waves) * steps * t_kb + 2500.0;
-  if (sp > 1) cyc += 1500.0 + 2.0 * kTileM * bn * 4.0 / 96.0;
+  const double ingest = (kTileM * 128.0 + wrows * 128.0) / 44.0;
+  const double handshake = bn >= 256 ? 880.0 : bn >= 128 ? 550.0 : 500.0;
+  const double t_kb = fmax(fmax(ingest, 2.0 * bn), handshake);
+  const double out = sp > 1 ? rows * bn * 4.0 * (sp - 1) / sp / 18.0 + 2500.0 : rows * bn * 2.0 / 24.0;
+  const double cyc = static_cast<double>(waves) * (steps * t_kb + 4000.0 + out);
   const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K;
   return fmax(cyc, bytes / 6.5e12 * 1.9e9);
 }
