@@ -117,6 +117,7 @@ struct Params {
   int M, N, K, KB;
   int split;
   int w_packed;
+  int w_static;                // weights and w_scale are not written by the preceding kernel
   uint64_t timeout_ns;
 };
 
@@ -237,6 +238,21 @@ __device__ __forceinline__ void with_split(int S, F&& body) {
   }
 }
 
+// TMA of one K block of a BN-row weight tile starting at weight row wr0:
+// packed layout (tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128)
+// or row-major [N, K].
+template <int WROWS>
+__device__ __forceinline__ void load_w_tile(uint32_t dst, const CUtensorMap* map, uint32_t bar, const Params& p,
+                                            int wr0, int kb, uint64_t pol) {
+  if (p.w_packed) {
+#pragma unroll
+    for (int t = 0; t < (WROWS + 127) / 128; ++t)
+      tma_load_2d(dst + t * 16384, map, bar, 0, (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol);
+  } else {
+    tma_load_2d(dst, map, bar, kb * kBlk, wr0, pol);
+  }
+}
+
 // PAIR = false: one CTA per 128-token x BN-weight-row tile (cta_group::1).
 // PAIR = true : two CTAs (cluster x pair) share a 256-token x BN tile through
 //   tcgen05 cta_group::2: each CTA loads its own 128 tokens and half of the
@@ -343,8 +359,22 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   tc_fence_after();
   // Everything above touches only this CTA's own resources, so with
-  // programmatic dependent launch it overlaps the previous kernel's tail;
-  // nothing the previous kernel may have written is read before this wait.
+  // programmatic dependent launch it overlaps the previous kernel's tail.
+  // With static weights (the caller guarantees the preceding kernel does not
+  // write WQ), the first ring stages of weight tiles are requested before the
+  // dependency wait as well; activations, scales and every store still wait.
+  int prefetched = 0;  // stages whose weight tiles were issued before the wait
+  if constexpr (!PAIR) {
+    if (p.w_static && warp == 0 && lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      prefetched = nk < C::kStages ? nk : C::kStages;
+      for (int i = 0; i < prefetched; ++i) {
+        const uint32_t sb = base + C::kOffB + i * C::kBBytes;
+        mbar_arrive_expect_tx(bar_full(i), C::kStageBytes);
+        load_w_tile<C::kWRows>(sb, &tmap_w, bar_full(i), p, n0, kb0 + i, pol_w);
+      }
+    }
+  }
   grid_dependency_wait();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t tmo = p.timeout_ns;
@@ -382,17 +412,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
               tma_load_2d_pair(sb, &tmap_w, fb, kb * kBlk, wr0, pol_w);
             }
           } else {
-            mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+            if (i >= prefetched) mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
             tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
-            if (p.w_packed) {
-              // packed: tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128
-#pragma unroll
-              for (int t = 0; t < (C::kWRows + 127) / 128; ++t)
-                tma_load_2d(sb + t * 16384, &tmap_w, bar_full(st), 0,
-                            (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol_w);
-            } else {
-              tma_load_2d(sb, &tmap_w, bar_full(st), kb * kBlk, wr0, pol_w);
-            }
+            if (i >= prefetched) load_w_tile<C::kWRows>(sb, &tmap_w, bar_full(st), p, wr0, kb, pol_w);
           }
           produced = i + 1;
         }
@@ -1108,7 +1130,9 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
                     void* stream) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
   if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
-  if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
+  if (wq_packed & ~(FACK_W_PACKED | FACK_W_STATIC)) return FACK_ERR_BAD_ARG;
+  const int w_static = (wq_packed & FACK_W_STATIC) ? 1 : 0;
+  wq_packed &= FACK_W_PACKED;
   if (!xq || !wq || !out || !x_scale || !w_scale) return FACK_ERR_BAD_ALIGN;
   if (!aligned(xq, 16) || !aligned(wq, 16) || !aligned(out, 16) || !aligned(x_scale, 4) || !aligned(w_scale, 4))
     return FACK_ERR_BAD_ALIGN;
@@ -1152,6 +1176,7 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
   p.KB = KB;
   p.split = sp;
   p.w_packed = wq_packed;
+  p.w_static = w_static;
   p.timeout_ns = 2000000000ull;  // 2 s: far above any legitimate wait, short enough to report a lost arrival
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
