@@ -27,7 +27,6 @@ FACK_ERR_SCRATCH_LIMIT = 10
 
 FACK_W_ROW_MAJOR = 0
 FACK_W_PACKED = 1
-FACK_W_STATIC = 2
 
 # Every symbol the header declares, with its ctypes signature.
 _c_int, _c_i64, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t

@@ -117,7 +117,6 @@ struct Params {
   int M, N, K, KB;
   int split;
   int w_packed;
-  int w_static;                // weights and w_scale are not written by the preceding kernel
   uint64_t timeout_ns;
 };
 
@@ -176,21 +175,30 @@ __device__ __noinline__ void reduce_dsmem(uint32_t stg, int rank0, int rank_step
   }
 }
 
-// Copy the staged fp32 partial (valid rows) to its workspace slot.
+// Copy the staged fp32 partial to its workspace slot: the valid rows other
+// slices reduce (every row outside [keep0, keep1), which this CTA reduces
+// from its own staging).  An SM stores at only ~24 B/clk, so nothing is
+// written that no other CTA reads.
 template <int BN, int PITCH>
-__device__ __noinline__ void copy_partial(const float* stg, int rows, float* part) {
+__device__ __noinline__ void copy_partial(const float* stg, int rows, int keep0, int keep1, float* part) {
   constexpr int kRowF4 = BN / 4;
-  for (int c = threadIdx.x; c < rows * kRowF4; c += kThreads) {
-    const int r = c / kRowF4, c4 = c % kRowF4;
+  const int kept = keep1 > keep0 ? keep1 - keep0 : 0;
+  for (int c = threadIdx.x; c < (rows - kept) * kRowF4; c += kThreads) {
+    int r = c / kRowF4;
+    r += r >= keep0 ? kept : 0;
+    const int c4 = c % kRowF4;
     __stcg(reinterpret_cast<float4*>(part + r * BN + c4 * 4),
            *reinterpret_cast<const float4*>(stg + r * PITCH + c4 * 4));
   }
 }
 
-// Split-K reduction from the workspace: rows [r0, r1), slices in order, with
-// the loads of U items x S slices in flight per thread (as reduce_dsmem).
-template <int BN, int S>
-__device__ __noinline__ void reduce_global(const float* part0, int r0, int r1, __nv_bfloat16* out, int64_t ldo) {
+// Split-K reduction through the workspace: rows [r0, r1), slices in order
+// 0..S-1; slice `self` comes from this CTA's own staging tile (pitch PITCH),
+// the others from the workspace (L2).  Loads of U items x S slices are in
+// flight per thread before any is added (as reduce_dsmem).
+template <int BN, int PITCH, int S>
+__device__ __noinline__ void reduce_global(const float* part0, const float* stg, int self, int r0, int r1,
+                                           __nv_bfloat16* out, int64_t ldo) {
   constexpr int kRowF4 = BN / 4;
   constexpr int U = (24 / S) > 1 ? 24 / S : 1;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
@@ -199,11 +207,12 @@ __device__ __noinline__ void reduce_global(const float* part0, int r0, int r1, _
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int it = it0 + u * kThreads;
-      const float* src = part0 + (r0 + it / kRowF4) * BN + (it % kRowF4) * 4;
+      const int r = r0 + it / kRowF4, c = (it % kRowF4) * 4;
       if (it < items) {
 #pragma unroll
         for (int t = 0; t < S; ++t)
-          v[u][t] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(t) * kTileM * BN));
+          v[u][t] = t == self ? *reinterpret_cast<const float4*>(stg + r * PITCH + c)
+                              : __ldcg(reinterpret_cast<const float4*>(part0 + (static_cast<int64_t>(t) * kTileM + r) * BN + c));
       }
     }
 #pragma unroll
@@ -359,22 +368,8 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   tc_fence_after();
   // Everything above touches only this CTA's own resources, so with
-  // programmatic dependent launch it overlaps the previous kernel's tail.
-  // With static weights (the caller guarantees the preceding kernel does not
-  // write WQ), the first ring stages of weight tiles are requested before the
-  // dependency wait as well; activations, scales and every store still wait.
-  int prefetched = 0;  // stages whose weight tiles were issued before the wait
-  if constexpr (!PAIR) {
-    if (p.w_static && warp == 0 && lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      prefetched = nk < C::kStages ? nk : C::kStages;
-      for (int i = 0; i < prefetched; ++i) {
-        const uint32_t sb = base + C::kOffB + i * C::kBBytes;
-        mbar_arrive_expect_tx(bar_full(i), C::kStageBytes);
-        load_w_tile<C::kWRows>(sb, &tmap_w, bar_full(i), p, n0, kb0 + i, pol_w);
-      }
-    }
-  }
+  // programmatic dependent launch it overlaps the previous kernel's tail;
+  // nothing the previous kernel may have written is read before this wait.
   grid_dependency_wait();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t tmo = p.timeout_ns;
@@ -412,9 +407,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
               tma_load_2d_pair(sb, &tmap_w, fb, kb * kBlk, wr0, pol_w);
             }
           } else {
-            if (i >= prefetched) mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+            mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
             tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
-            if (i >= prefetched) load_w_tile<C::kWRows>(sb, &tmap_w, bar_full(st), p, wr0, kb, pol_w);
+            load_w_tile<C::kWRows>(sb, &tmap_w, bar_full(st), p, wr0, kb, pol_w);
           }
           produced = i + 1;
         }
@@ -565,6 +560,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // Undo the register split: the rescale warpgroups give back what they took
   // before the control warpgroup reclaims it, so the teardown (drain, staged
   // copy-out, split-K reduction) runs with the launch allocation in every warp.
+  // setmaxnreg is .sync.aligned and lane 0 of the producer and MMA warps has
+  // just left a loop that the other lanes skipped: reconverge first.
+  __syncwarp();
   if (warp >= kEpiWarp0)
     regs_dec<kLaunchRegs>();
   else
@@ -653,19 +651,21 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     cluster_sync_all();
     return;
   }
-  // Caller-provided workspace: copy the staged partial there (L2), publish it
-  // with the cluster barrier, and reduce from global memory.
+  // Caller-provided workspace (reduce-scatter through L2): each slice writes
+  // the rows the other slices reduce, the cluster barrier publishes them, and
+  // each slice sums its own rows from the workspace and its own staging.  No
+  // CTA reads another's shared memory, so there is no second barrier.
   const int64_t tile = static_cast<int64_t>(mt) * (p.N / BN) + nt;
+  const float* stg32 = reinterpret_cast<const float*>(smem + C::kOffA);
   if (ok) {
-    copy_partial<BN, C::kPitch32>(reinterpret_cast<const float*>(smem + C::kOffA), rows_v,
-                                  p.partials + (tile * S + s) * kTileM * BN);
+    copy_partial<BN, C::kPitch32>(stg32, rows_v, r0, r1, p.partials + (tile * S + s) * kTileM * BN);
     __threadfence();
   }
   cluster_sync_all();
   if (!ok) return;
   with_split(S, [&](auto sc) {
-    reduce_global<BN, decltype(sc)::value>(p.partials + tile * S * kTileM * BN, r0, r1,
-                                           p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+    reduce_global<BN, C::kPitch32, decltype(sc)::value>(p.partials + tile * S * kTileM * BN, stg32, s, r0, r1,
+                                                        p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
   });
 }
 
@@ -1130,9 +1130,7 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
                     void* stream) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
   if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
-  if (wq_packed & ~(FACK_W_PACKED | FACK_W_STATIC)) return FACK_ERR_BAD_ARG;
-  const int w_static = (wq_packed & FACK_W_STATIC) ? 1 : 0;
-  wq_packed &= FACK_W_PACKED;
+  if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
   if (!xq || !wq || !out || !x_scale || !w_scale) return FACK_ERR_BAD_ALIGN;
   if (!aligned(xq, 16) || !aligned(wq, 16) || !aligned(out, 16) || !aligned(x_scale, 4) || !aligned(w_scale, 4))
     return FACK_ERR_BAD_ALIGN;
@@ -1176,7 +1174,6 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
   p.KB = KB;
   p.split = sp;
   p.w_packed = wq_packed;
-  p.w_static = w_static;
   p.timeout_ns = 2000000000ull;  // 2 s: far above any legitimate wait, short enough to report a lost arrival
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -384,7 +384,10 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 }
 
 // --------------------------------------------------------------- clusters --
+// barrier.cluster.*.aligned: every lane of the warp must execute it together,
+// so reconverge first (callers reach it after per-lane loops).
 __device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
   asm volatile(
       "barrier.cluster.arrive.release.aligned;\n\t"
       "barrier.cluster.wait.acquire.aligned;" ::

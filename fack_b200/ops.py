@@ -146,12 +146,10 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
 
 
 def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m=0, tile_n=0,
-            reduce="dsmem", static_weights=False):
+            reduce="dsmem"):
     """reduce = "dsmem": split-K slices combine through the cluster's shared
     memory (no workspace, nothing allocated); "global": through a cached
-    workspace in global memory.  static_weights: the kernel preceding this
-    call on the stream does not write ``wq`` (FACK_W_STATIC), so the GEMM may
-    start fetching weights before it has finished."""
+    workspace in global memory."""
     M, K = xq.shape
     N = wq.shape[0]
     dev = xq.device
@@ -160,8 +158,7 @@ def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m
         tm, tn, sk, need = plan(M, N, K, tile_m, tile_n, split_k)
         ws = _workspace(dev, need) if reduce == "global" else None
         st = lib.fack_gemm_bs_ex(
-            xq.data_ptr(), xq.stride(0), wq.data_ptr(),
-            (_lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR) | (_lib.FACK_W_STATIC if static_weights else 0),
+            xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
             x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0),
             M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
     _lib.check(st, "fack_gemm_bs_ex")
@@ -170,15 +167,11 @@ def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                     out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0, tile_m: int = 0,
-                    reduce: str = "dsmem", static_weights: Optional[bool] = None) -> torch.Tensor:
+                    reduce: str = "dsmem") -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
     :func:`shuffle_weight` (detected by its ``is_shuffled`` mark).
-    ``static_weights`` (default: True for :func:`shuffle_weight` outputs, which
-    are model weights) lets the kernel fetch weights before the preceding
-    kernel on the stream has finished; pass False if that kernel writes ``wq``
-    after signalling programmatic dependents.
     """
     if xq.dim() != 2 or wq.dim() != 2:
         raise ValueError("XQ and WQ must be 2-D")
@@ -196,9 +189,8 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
         sm = max(sm, 1)
     if reduce not in ("dsmem", "global"):
         raise ValueError("reduce must be 'dsmem' or 'global'")
-    packed = bool(getattr(wq, "is_shuffled", False))
-    return _launch(xq, wq, packed, x_scale, sm, sk, w_scale, out, split_k, tile_m, tile_n, reduce,
-                   packed if static_weights is None else bool(static_weights))
+    return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_m,
+                   tile_n, reduce)
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):
@@ -239,8 +231,7 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     _check_common(a, b, w_scale, out, M, N, K)
     sm, sk = _aiter_xscale_strides(x_scale, M, K // BLOCK)
     split = name_split if splitK is None else int(splitK)
-    # preshuffled weights are model weights: no kernel before the GEMM writes them
-    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_m, tile_n, static_weights=shuffled)
+    return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_m, tile_n)
 
 
 def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bfloat16):

@@ -47,17 +47,10 @@ enum fack_status {
   FACK_ERR_SCRATCH_LIMIT = 10   /* fack_gemm_bs_noalloc: built-in scratch too small */
 };
 
-/* Weight layouts accepted by fack_gemm_bs (argument `wq_packed`), optionally
- * OR-ed with FACK_W_STATIC. */
+/* Weight layouts accepted by fack_gemm_bs (argument `wq_packed`). */
 enum fack_w_layout {
   FACK_W_ROW_MAJOR = 0,  /* WQ[N,K], row stride K bytes                       */
-  FACK_W_PACKED = 1,     /* output of fack_gemm_bs_prepack_w                   */
-  /* The kernel that precedes this call in the stream does not write WQ (model
-   * weights): the GEMM may request its first weight tiles before that kernel
-   * has finished (programmatic dependent launch).  Activations and scales are
-   * still read only after it has finished.  Leave it unset when the preceding
-   * kernel writes WQ after signalling its dependents early. */
-  FACK_W_STATIC = 2
+  FACK_W_PACKED = 1      /* output of fack_gemm_bs_prepack_w                   */
 };
 
 /* Human-readable text for a status code (static storage, never NULL). */

@@ -99,10 +99,7 @@ def test_pointer_and_stride_checks_before_device():
     assert lib.fack_gemm_bs(ok, K, ok, 0, ok, 1, 1, ok, ok, N + 4, M, N, K, 1, None, 0, None) == _lib.FACK_ERR_BAD_STRIDE
     assert lib.fack_gemm_bs(ok, K, ok, 0, ok, 0, 1, ok, ok, N, M, N, K, 1, None, 0, None) == _lib.FACK_ERR_BAD_STRIDE
     # layout / split arguments
-    # wq_packed: layout bit 0 plus FACK_W_STATIC; any other bit is rejected
-    assert lib.fack_gemm_bs(ok, K, ok, 4, ok, 1, 1, ok, ok, N, M, N, K, 1, None, 0, None) == _lib.FACK_ERR_BAD_ARG
-    assert lib.fack_gemm_bs(ok, K, ok, _lib.FACK_W_PACKED | _lib.FACK_W_STATIC | 8, ok, 1, 1, ok, ok, N, M, N, K, 1,
-                            None, 0, None) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs(ok, K, ok, 2, ok, 1, 1, ok, ok, N, M, N, K, 1, None, 0, None) == _lib.FACK_ERR_BAD_ARG
     assert lib.fack_gemm_bs(ok, K, ok, 0, ok, 1, 1, ok, ok, N, M, N, K, 9, None, 0, None) == _lib.FACK_ERR_BAD_ARG
     # prepack and interleave validation
     assert lib.fack_gemm_bs_prepack_w(ok, K, None, 100, K, ok, None, None) == _lib.FACK_ERR_BAD_SHAPE

@@ -130,29 +130,6 @@ def test_split_k_is_deterministic(cuda_device, decode_weights):
     assert_close(first, orc.reference_gemm(xq, wq, xs, ws), "decode")
 
 
-@pytest.mark.parametrize("packed", [False, True])
-@pytest.mark.parametrize("K,split", [(256, 1), (7168, 1), (7168, 4)])
-def test_static_weight_prefetch_is_bitwise_neutral(cuda_device, packed, K, split):
-    """FACK_W_STATIC (weight tiles requested before the dependency wait) gives
-    the same bits as the plain path, with fewer K blocks than ring stages
-    (K=256) and more; launched back to back so the next GEMM starts while the
-    previous one is still finishing."""
-    d = cuda_device
-    M, N = 200, 1024
-    xq, xs = data.make_activations(M, K, "normal", seed=5)
-    wq, ws = data.make_weights(N, K, "normal", seed=6)
-    xq, xs, ws = xq.to(d), xs.to(d), ws.to(d)
-    w = fb.shuffle_weight(wq.to(d)) if packed else wq.to(d)
-    plain = fb.gemm_blockscale(xq, w, xs, ws, split_k=split, static_weights=False)
-    outs = [poisoned(M, N, d) for _ in range(6)]
-    for o in outs:
-        fb.gemm_blockscale(xq, w, xs, ws, out=o, split_k=split, static_weights=True)
-    torch.cuda.synchronize()
-    for o in outs:
-        assert torch.equal(o.view(torch.int16), plain.view(torch.int16))
-    assert_close(plain, orc.reference_gemm(xq.cpu(), wq, xs.cpu(), ws.cpu()), "static-weight path")
-
-
 def test_runner_protocol_graph_replay(cuda_device):
     """client/aiter/runner.py:139-188: two seeds, poison, graph of iters launches, poison, replay, re-check."""
     d = cuda_device
