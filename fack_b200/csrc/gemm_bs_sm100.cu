@@ -43,7 +43,6 @@
 #include <string.h>
 
 #include <mutex>
-#include <type_traits>
 
 #include "../../include/fack_gemm.h"
 #include "sm100_ptx.cuh"
@@ -131,47 +130,27 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float4& v
 
 // Split-K reduction over distributed shared memory: rows [r0, r1) of the
 // tile, summed over the S cluster CTAs' staged fp32 partials in rank order.
-// A remote shared-memory load costs several hundred cycles, so each thread
-// first issues the loads of U items x S slices (<= 24 x 16 B in flight) and
-// only then adds them, slice by slice in fixed order.  Kept out of line so
-// its registers are allocated apart from the rescale loop; it runs after the
-// register split has been undone (every warp at the launch allocation).
-template <int BN, int PITCH, int S>
-__device__ __noinline__ void reduce_dsmem(uint32_t stg, int rank0, int rank_step, int r0, int r1,
+// One remote load per slice per item in flight: the pull is bound by the
+// distributed-shared-memory bandwidth, not by latency.  Kept out of line so
+// its registers are allocated apart from the rescale loop.
+template <int BN, int PITCH>
+__device__ __noinline__ void reduce_dsmem(uint32_t stg, int S, int rank0, int rank_step, int r0, int r1,
                                           __nv_bfloat16* out, int64_t ldo) {
   constexpr int kRowF4 = BN / 4;
-  constexpr int U = (24 / S) > 1 ? 24 / S : 1;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
-  uint32_t peer[S];
-#pragma unroll
-  for (int t = 0; t < S; ++t) peer[t] = dsmem_map(stg, rank0 + t * rank_step);
-  for (int it0 = threadIdx.x; it0 < items; it0 += U * kThreads) {
-    float4 v[U][S];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + u * kThreads;
-      const int r = r0 + it / kRowF4;
-      const uint32_t off = static_cast<uint32_t>((r * PITCH + (it % kRowF4) * 4) * 4);
-      if (it < items) {
-#pragma unroll
-        for (int t = 0; t < S; ++t) v[u][t] = dsmem_ld4(peer[t] + off);
-      }
+  for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int r = r0 + it / kRowF4;
+    const int c4 = it % kRowF4;
+    const uint32_t addr = stg + static_cast<uint32_t>((r * PITCH + c4 * 4) * 4);
+    float4 sum = dsmem_ld4(dsmem_map(addr, rank0));
+    for (int t = 1; t < S; ++t) {
+      const float4 v = dsmem_ld4(dsmem_map(addr, rank0 + t * rank_step));
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + u * kThreads;
-      if (it < items) {
-        float4 sum = v[u][0];
-#pragma unroll
-        for (int t = 1; t < S; ++t) {
-          sum.x += v[u][t].x;
-          sum.y += v[u][t].y;
-          sum.z += v[u][t].z;
-          sum.w += v[u][t].w;
-        }
-        store_bf16x4(out + (r0 + it / kRowF4) * ldo + (it % kRowF4) * 4, sum);
-      }
-    }
+    store_bf16x4(out + r * ldo + c4 * 4, sum);
   }
 }
 
@@ -194,56 +173,29 @@ __device__ __noinline__ void copy_partial(const float* stg, int rows, int keep0,
 
 // Split-K reduction through the workspace: rows [r0, r1), slices in order
 // 0..S-1; slice `self` comes from this CTA's own staging tile (pitch PITCH),
-// the others from the workspace (L2).  Loads of U items x S slices are in
-// flight per thread before any is added (as reduce_dsmem).
-template <int BN, int PITCH, int S>
-__device__ __noinline__ void reduce_global(const float* part0, const float* stg, int self, int r0, int r1,
+// the others from the workspace (L2).
+template <int BN, int PITCH>
+__device__ __noinline__ void reduce_global(const float* part0, const float* stg, int self, int S, int r0, int r1,
                                            __nv_bfloat16* out, int64_t ldo) {
   constexpr int kRowF4 = BN / 4;
-  constexpr int U = (24 / S) > 1 ? 24 / S : 1;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
-  for (int it0 = threadIdx.x; it0 < items; it0 += U * kThreads) {
-    float4 v[U][S];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + u * kThreads;
-      const int r = r0 + it / kRowF4, c = (it % kRowF4) * 4;
-      if (it < items) {
-#pragma unroll
-        for (int t = 0; t < S; ++t)
-          v[u][t] = t == self ? *reinterpret_cast<const float4*>(stg + r * PITCH + c)
-                              : __ldcg(reinterpret_cast<const float4*>(part0 + (static_cast<int64_t>(t) * kTileM + r) * BN + c));
+  for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int r = r0 + it / kRowF4;
+    const int c = (it % kRowF4) * 4;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < S; ++t) {
+      const float4 v = t == self ? *reinterpret_cast<const float4*>(stg + r * PITCH + c)
+                                 : __ldcg(reinterpret_cast<const float4*>(part0 + (static_cast<int64_t>(t) * kTileM + r) * BN + c));
+      if (t == 0) {
+        sum = v;
+      } else {
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
       }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + u * kThreads;
-      if (it < items) {
-        float4 sum = v[u][0];
-#pragma unroll
-        for (int t = 1; t < S; ++t) {
-          sum.x += v[u][t].x;
-          sum.y += v[u][t].y;
-          sum.z += v[u][t].z;
-          sum.w += v[u][t].w;
-        }
-        store_bf16x4(out + (r0 + it / kRowF4) * ldo + (it % kRowF4) * 4, sum);
-      }
-    }
-  }
-}
-
-// Run body<S>() for the runtime slice count 2..kMaxSplit.
-template <typename F>
-__device__ __forceinline__ void with_split(int S, F&& body) {
-  switch (S) {
-    case 2: body(std::integral_constant<int, 2>{}); break;
-    case 3: body(std::integral_constant<int, 3>{}); break;
-    case 4: body(std::integral_constant<int, 4>{}); break;
-    case 5: body(std::integral_constant<int, 5>{}); break;
-    case 6: body(std::integral_constant<int, 6>{}); break;
-    case 7: body(std::integral_constant<int, 7>{}); break;
-    default: body(std::integral_constant<int, 8>{}); break;
+    store_bf16x4(out + r * ldo + c, sum);
   }
 }
 
@@ -557,16 +509,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // The next launch may start its prologue now; it still waits for this whole
   // grid to finish before reading anything (grid_dependency_wait).
   grid_launch_dependents();
-  // Undo the register split: the rescale warpgroups give back what they took
-  // before the control warpgroup reclaims it, so the teardown (drain, staged
-  // copy-out, split-K reduction) runs with the launch allocation in every warp.
-  // setmaxnreg is .sync.aligned and lane 0 of the producer and MMA warps has
-  // just left a loop that the other lanes skipped: reconverge first.
-  __syncwarp();
-  if (warp >= kEpiWarp0)
-    regs_dec<kLaunchRegs>();
-  else
-    regs_inc<kLaunchRegs>();
+  __syncwarp();  // lane 0 of the producer and MMA warps rejoins the other lanes
   tc_fence_before();
   __syncthreads();  // every role of this CTA has left its loop
   tc_fence_after();
@@ -644,10 +587,8 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // its shared memory) alive until all peers have finished reading.
     cluster_sync_all();
     if (ok)
-      with_split(S, [&](auto sc) {
-        reduce_dsmem<BN, C::kPitch32, decltype(sc)::value>(base + C::kOffA, rank0, rank_step, r0, r1,
-                                                          p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
-      });
+      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1,
+                                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
     cluster_sync_all();
     return;
   }
@@ -663,10 +604,8 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   cluster_sync_all();
   if (!ok) return;
-  with_split(S, [&](auto sc) {
-    reduce_global<BN, C::kPitch32, decltype(sc)::value>(p.partials + tile * S * kTileM * BN, stg32, s, r0, r1,
-                                                        p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
-  });
+  reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1,
+                                 p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
 }
 
 // ------------------------------------------------------------------ prepack --
