@@ -340,7 +340,11 @@ def run_ours(args):
     peaks = measured_peaks()
     k_bytes = data.algorithmic_bytes(wl.M, n_local, wl.K)
     k_flops = data.flops(wl.M, n_local, wl.K)
-    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    # a timed region of more than ~0.2 s runs under the power cap: compare
+    # with the sustained GEMM figure, a short burst with the burst figure
+    sustained = ms > 200.0
+    bf16_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    fp8_peak = 2.0 * bf16_peak
     t_mem = k_bytes / (peaks["hbm_gbs"] * 1e3)        # us
     t_tc = k_flops / (fp8_peak * 1e6)                 # us
     hbm_gbs = k_bytes / (k_us * 1e3)
@@ -353,8 +357,8 @@ def run_ours(args):
                 "frac": round(tflops_k / fp8_peak, 4)}
     roof.update({"traffic": load_traffic(args.workload), "algorithmic_bytes": k_bytes,
                  "kernel_us": round(k_us, 3), "peak_source": (
-                     f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 burst "
-                     f"{peaks['bf16_tflops']} TFLOP/s"),
+                     f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 "
+                     f"{'sustained' if sustained else 'burst'} {bf16_peak} TFLOP/s (timed region {ms:.0f} ms)"),
                  "t_mem_us": round(t_mem, 3), "t_tc_us": round(t_tc, 3),
                  "frac_of_max_roof": round(max(t_mem, t_tc) / k_us, 4)})
 
