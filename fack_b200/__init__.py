@@ -14,6 +14,7 @@ from .ops import (  # noqa: F401
     gemm_a8w8_blockscale_bpreshuffle_asm,
     gemm_blockscale,
     get_config,
+    quantize_activations,
     shuffle_weight,
     workspace_size,
 )
@@ -26,6 +27,7 @@ __all__ = [
     "gemm_a8w8_blockscale_bpreshuffle_asm",
     "gemm_blockscale",
     "get_config",
+    "quantize_activations",
     "shuffle_weight",
     "workspace_size",
 ]

@@ -28,6 +28,9 @@ FACK_ERR_SCRATCH_LIMIT = 10
 FACK_W_ROW_MAJOR = 0
 FACK_W_PACKED = 1
 
+FACK_DTYPE_F32 = 0
+FACK_DTYPE_BF16 = 1
+
 # Every symbol the header declares, with its ctypes signature.
 _c_int, _c_i64, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t
 SIGNATURES = {
@@ -47,6 +50,7 @@ SIGNATURES = {
     "fack_gemm_bs_noalloc": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                                       _c_int, _c_int, _c_int, _c_int, _c_p]),
     "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
+    "fack_quant_act": (_c_int, [_c_p, _c_int, _c_i64, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p]),
     "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
 }
 

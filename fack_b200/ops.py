@@ -249,6 +249,41 @@ def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bf
                                                 cfg["kernelName"], bool(getattr(weight, "is_shuffled", False)))
 
 
+def quantize_activations(x: torch.Tensor, layout: str = "aiter"):
+    """Fused activation quantisation for the GEMM (``fack_quant_act``).
+
+    ``x``: fp32 or bf16 CUDA tensor [M, K], K % 128 == 0, unit stride along K.
+    Returns ``(xq, x_scale)``: e4m3 codes [M, K] and fp32 scales, one per token
+    per 128-wide K group (scale = amax/240, the benchmark construction).
+    ``layout="aiter"`` gives x_scale as the reference's transposed-contiguous
+    view (``sa.T.contiguous().view_as(sa)``, client/aiter/hsa/gfx942/driver.py:22),
+    ready for :func:`gemm_a8w8_blockscale_bpreshuffle_asm`; ``"logical"`` gives
+    a row-major [M, K/128] tensor for :func:`gemm_blockscale`.
+    """
+    if x.dim() != 2 or not x.is_cuda:
+        raise ValueError("x must be a 2-D CUDA tensor")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("x must be float32 or bfloat16")
+    if layout not in ("aiter", "logical"):
+        raise ValueError("layout must be 'aiter' or 'logical'")
+    M, K = x.shape
+    if K % BLOCK:
+        raise ValueError("K must be a multiple of 128")
+    if x.stride(1) != 1:
+        raise ValueError("x must be contiguous along K")
+    dev = x.device
+    xq = torch.empty((M, K), dtype=FP8, device=dev)
+    xs = torch.empty((M, K // BLOCK), dtype=torch.float32, device=dev)
+    sm, sk = (1, M) if layout == "aiter" else (K // BLOCK, 1)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.fack_quant_act(x.data_ptr(), _lib.FACK_DTYPE_F32 if x.dtype == torch.float32 else _lib.FACK_DTYPE_BF16,
+                                x.stride(0), M, K, xq.data_ptr(), xq.stride(0), xs.data_ptr(), sm, sk,
+                                _stream_handle(dev))
+    _lib.check(st, "fack_quant_act")
+    return xq, xs
+
+
 def shuffle_weight(b: torch.Tensor, layout=(16, 16)) -> torch.Tensor:
     """Pre-pack an e4m3 ``[N, K]`` weight into this library's tile layout.
 

@@ -53,6 +53,12 @@ enum fack_w_layout {
   FACK_W_PACKED = 1      /* output of fack_gemm_bs_prepack_w                   */
 };
 
+/* Element types of the activation input to fack_quant_act (argument `x_dtype`). */
+enum fack_dtype {
+  FACK_DTYPE_F32 = 0,    /* fp32                                               */
+  FACK_DTYPE_BF16 = 1    /* bf16                                               */
+};
+
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* fack_status_string(int status);
 
@@ -197,6 +203,23 @@ int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_pac
  */
 int fack_gather_interleave(const void* gathered, int g, int M, int n_shard,
                            void* out, int64_t ldo, void* stream);
+
+/*
+ * Fused activation quantisation producing the GEMM's XQ and x_scale in one
+ * pass over X (fp32 or bf16 [M, K], row stride ldx elements):
+ *   x_scale[m, kb] = amax(|X[m, kb*128 .. kb*128+127]|) / 240  (1 if all zero)
+ *   xq[m, k]       = e4m3fn(clamp(X[m, k] / x_scale[m, k/128], -240, 240))
+ * (round to nearest even), the construction of the benchmark inputs; bf16
+ * input is widened to fp32 first.  x_scale element (m, kb) is written at
+ * x_scale[m*xs_stride_m + kb*xs_stride_kb], so the reference's
+ * transposed-contiguous view sa.T.contiguous().view_as(sa)
+ * (client/aiter/hsa/gfx942/driver.py:22) is xs_stride_m = 1,
+ * xs_stride_kb = M.  K % 128 == 0; x 16-byte aligned with ldx % 8 == 0;
+ * xq 16-byte aligned with ldq % 16 == 0.  The reference takes X already
+ * quantised (driver.py:14-17); this is the step before the GEMM, fused.
+ */
+int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, int K, void* xq, int64_t ldq,
+                   float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb, void* stream);
 
 /*
  * Reads (and with reset != 0 clears) the current device's error word, which a

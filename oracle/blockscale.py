@@ -63,3 +63,26 @@ def unpack_aiter_xscale(packed_sa: torch.Tensor) -> torch.Tensor:
     (inverse of ``sa.T.contiguous().view_as(sa)``, driver.py:22)."""
     M, KB = packed_sa.shape
     return packed_sa.contiguous().view(KB, M).t().contiguous()
+
+
+QMAX = 240.0
+
+
+def quantize_activations_ref(x: torch.Tensor):
+    """(XQ e4m3 [M,K], logical x_scale fp32 [M,K/128]) from fp32 or bf16 X.
+
+    The activation construction of the benchmark configs (BASELINE's
+    "quantised per row per 128-K group with x_scale = amax/240"): per token
+    and 128-wide K group, scale = amax(|x|)/240 (1 for an all-zero group),
+    code = e4m3fn(clamp(x/scale, -240, 240)) rounded to nearest even; bf16
+    input is widened to fp32 first.  The reference takes X already quantised
+    (client/aiter/hsa/gfx942/driver.py:14-17); this restates the step before
+    its GEMM, which fack_quant_act fuses into one kernel.
+    """
+    x = x.float().cpu()
+    M, K = x.shape
+    g = x.reshape(M, K // BLOCK, BLOCK)
+    amax = g.abs().amax(dim=2)
+    scale = torch.where(amax > 0, amax / QMAX, torch.ones_like(amax))
+    q = (g / scale.unsqueeze(2)).clamp(-QMAX, QMAX).to(torch.float8_e4m3fn)
+    return q.reshape(M, K), scale.contiguous()

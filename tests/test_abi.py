@@ -107,6 +107,13 @@ def test_pointer_and_stride_checks_before_device():
     assert lib.fack_gather_interleave(ok, 2, 4, 12, ok, 24, None) == _lib.FACK_ERR_BAD_SHAPE
     assert lib.fack_gather_interleave(ok, 2, 4, 128, ok, 200, None) == _lib.FACK_ERR_BAD_STRIDE
     assert lib.fack_device_status(None, None, 0) == _lib.FACK_ERR_BAD_ARG
+    # activation quantisation validation
+    f32, bf16 = _lib.FACK_DTYPE_F32, _lib.FACK_DTYPE_BF16
+    assert lib.fack_quant_act(ok, f32, K, M, 100, ok, K, ok, 1, M, None) == _lib.FACK_ERR_BAD_SHAPE
+    assert lib.fack_quant_act(ok, 7, K, M, K, ok, K, ok, 1, M, None) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_quant_act(ok + 4, bf16, K, M, K, ok, K, ok, 1, M, None) == _lib.FACK_ERR_BAD_ALIGN
+    assert lib.fack_quant_act(ok, f32, K + 4, M, K, ok, K, ok, 1, M, None) == _lib.FACK_ERR_BAD_STRIDE
+    assert lib.fack_quant_act(ok, f32, K, M, K, ok, K + 8, ok, 1, M, None) == _lib.FACK_ERR_BAD_STRIDE
 
 
 def test_check_maps_contract_violations_to_valueerror():
