@@ -1169,6 +1169,19 @@ int fack_gather_interleave(const void* gathered, int g, int M, int n_shard, void
   return cudaGetLastError() == cudaSuccess ? FACK_OK : FACK_ERR_LAUNCH;
 }
 
+}  // extern "C"
+
+namespace fack {
+// Device address of the status word on the current device, for the other
+// kernels of the library that report bounded-wait timeouts through it.
+unsigned int* device_status_word() {
+  void* p = nullptr;
+  return cudaGetSymbolAddress(&p, g_status) == cudaSuccess ? static_cast<unsigned int*>(p) : nullptr;
+}
+}  // namespace fack
+
+extern "C" {
+
 int fack_device_status(void* stream, unsigned int* flags, int reset) {
   if (!flags) return FACK_ERR_BAD_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

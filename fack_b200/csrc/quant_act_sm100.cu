@@ -9,126 +9,161 @@
 // transposed-contiguous view (client/aiter/hsa/gfx942/driver.py:22:
 // sa.T.contiguous().view_as(sa), i.e. stride_m = 1, stride_kb = M).
 //
-// HBM-bound byte work: a warp owns one 128-element group at a time (4
-// elements per lane, one 16 B or 8 B load), reduces the group's amax with
-// shuffles, divides with IEEE division, converts with the hardware
-// round-to-nearest-even e4m3 conversion and writes 4 codes per lane (128 B per
-// warp).  Each warp streams its own contiguous run of groups with 4 (fp32) or
-// 8 (bf16) groups in flight, so enough bytes are outstanding per SM to stream
-// at HBM rate.
+// HBM-bound byte work, staged through shared memory: two persistent CTAs per
+// SM; in each, one thread streams row chunks (up to 32 groups of 128 elements,
+// <= 16 KB) with 1-D bulk copies into a 4-stage ring, so the bytes in flight sit in
+// shared memory rather than registers; sixteen warps each take two groups at
+// a time from the landed chunk (4 elements per lane), reduce its amax with
+// shuffles, divide with IEEE division, convert with the hardware
+// round-to-nearest-even e4m3 conversion and store 4 codes per lane (128 B per
+// warp).  Every mbarrier wait is bounded; on expiry the CTA records a flag in
+// the library's device status word, drains its copies and exits.
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "../../include/fack_gemm.h"
+#include "sm100_ptx.cuh"
+
+namespace fack {
+unsigned int* device_status_word();  // gemm_bs_sm100.cu
+}
 
 namespace fack_quant {
 
+using namespace fack;
+
 constexpr int kBlk = 128;
 constexpr float kQmax = 240.0f;
-constexpr int kThreads = 256;
 
-// Raw 4-element loads (kept as loaded until used, so the bytes in flight cost
-// as few registers as possible) and their widening to fp32.
-struct Raw4F32 {
-  float4 r;
-};
-struct Raw4BF16 {
-  uint2 r;
-};
-__device__ __forceinline__ void load_raw(const float* p, Raw4F32& v) {
-  v.r = __ldcs(reinterpret_cast<const float4*>(p));  // streamed once
-}
-__device__ __forceinline__ void load_raw(const __nv_bfloat16* p, Raw4BF16& v) {
-  v.r = __ldcs(reinterpret_cast<const uint2*>(p));
-}
-__device__ __forceinline__ void widen(const Raw4F32& v, float (&f)[4]) {
-  f[0] = v.r.x;
-  f[1] = v.r.y;
-  f[2] = v.r.z;
-  f[3] = v.r.w;
-}
-__device__ __forceinline__ void widen(const Raw4BF16& v, float (&f)[4]) {
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.r.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.r.y));
-  f[0] = a.x;
-  f[1] = a.y;
-  f[2] = b.x;
-  f[3] = b.y;
-}
-template <typename T> struct RawOf;
-template <> struct RawOf<float> { using type = Raw4F32; };
-template <> struct RawOf<__nv_bfloat16> { using type = Raw4BF16; };
+constexpr int kStages = 4;
+constexpr int kChunkGroups = 32;                 // groups of 128 elements per chunk (one row segment)
+constexpr int kConsumerWarps = 16;
+constexpr int kQThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr unsigned kStQuant = 64u;               // status flag: a wait in the quantiser gave up
 
+// clamp(v / scale) to +-240 (IEEE division) and convert to e4m3 (round to
+// nearest even), two values per conversion; 4 codes packed little-endian
 __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float scale) {
-  uint32_t packed = 0;
+  float q[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float q = fminf(fmaxf(v[i] / scale, -kQmax), kQmax);
-    const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(q, __NV_SATFINITE, __NV_E4M3);
-    packed |= static_cast<uint32_t>(b) << (8 * i);
-  }
-  return packed;
+  for (int i = 0; i < 4; ++i) q[i] = fminf(fmaxf(v[i] / scale, -kQmax), kQmax);
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(q[0], q[1]), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(q[2], q[3]), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
 }
 
-// Groups in flight per warp: ~2 KB of input per warp keeps enough bytes
-// outstanding per SM to stream at HBM rate.
-template <typename T>
-struct InFlight {
-  static constexpr int value = 2048 / (kBlk * static_cast<int>(sizeof(T)));
-};
+__device__ __forceinline__ void lds4(uint32_t addr, const float*, float (&v)[4]) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "r"(addr));
+}
+__device__ __forceinline__ void lds4(uint32_t addr, const __nv_bfloat16*, float (&v)[4]) {
+  uint32_t lo, hi;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(addr));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) quant_act_kernel(const T* __restrict__ x, int64_t ldx, int M, int KB,
-                                                             uint8_t* __restrict__ xq, int64_t ldq,
-                                                             float* __restrict__ xs, int64_t xs_sm,
-                                                             int64_t xs_sk) {
-  constexpr int U = InFlight<T>::value;
-  using Raw = typename RawOf<T>::type;
-  const int lane = threadIdx.x & 31;
-  const int64_t groups = static_cast<int64_t>(M) * KB;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
-  const int64_t w = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  // each warp owns a contiguous run of groups (row-major over (m, kb)), so it
-  // streams one contiguous stretch of X and of the codes; (m, kb) advance by
-  // increments, with no division in the loop
-  const int64_t g_begin = w * groups / nwarps;
-  const int64_t g_end = (w + 1) * groups / nwarps;
-  int64_t m = g_begin / KB;
-  int kb = static_cast<int>(g_begin - m * KB);
-  for (int64_t g0 = g_begin; g0 < g_end; g0 += U) {
-    Raw raw[U];
-    const int64_t m0 = m;
-    const int kb0 = kb;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (g0 + u < g_end) load_raw(x + m * ldx + kb * kBlk + lane * 4, raw[u]);
-      if (++kb == KB) {
-        kb = 0;
-        ++m;
+__global__ void __launch_bounds__(kQThreads, 2) quant_act_kernel(const T* __restrict__ x, int64_t ldx, int M, int KB,
+                                                                 uint8_t* __restrict__ xq, int64_t ldq,
+                                                                 float* __restrict__ xs, int64_t xs_sm,
+                                                                 int64_t xs_sk, unsigned int* status,
+                                                                 uint64_t timeout_ns) {
+  constexpr int kChunkBytes = kChunkGroups * kBlk * static_cast<int>(sizeof(T));
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  __shared__ int abort_flag_s;
+  volatile int* abort_flag = &abort_flag_s;
+  const uint32_t ring = smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_row = (KB + kChunkGroups - 1) / kChunkGroups;     // chunks per row
+  const int64_t chunks = static_cast<int64_t>(M) * per_row;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_addr(&full[i]), 1);
+      mbar_init(smem_addr(&empty[i]), kConsumerWarps);
+    }
+    abort_flag_s = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      int64_t issued = 0;
+      for (int64_t c = blockIdx.x; c < chunks; c += gridDim.x, ++issued) {
+        const int st = static_cast<int>(issued % kStages);
+        const uint32_t ph = static_cast<uint32_t>(issued / kStages) & 1u;
+        if (!wait_bounded(smem_addr(&empty[st]), ph ^ 1u, abort_flag, status, kStQuant, timeout_ns)) break;
+        const int64_t m = c / per_row;
+        const int g0 = static_cast<int>(c - m * per_row) * kChunkGroups;
+        const int ng = KB - g0 < kChunkGroups ? KB - g0 : kChunkGroups;
+        const uint32_t bytes = static_cast<uint32_t>(ng) * kBlk * sizeof(T);
+        mbar_arrive_expect_tx(smem_addr(&full[st]), bytes);
+        bulk_load_1d(ring + st * kChunkBytes, x + m * ldx + static_cast<int64_t>(g0) * kBlk, bytes,
+                     smem_addr(&full[st]));
+      }
+      if (*abort_flag) {
+        // no copy may land after the CTA exits: wait (bounded, fresh deadline)
+        // for the last stages issued
+        volatile int no_abort = 0;
+        const int64_t first = issued > kStages ? issued - kStages : 0;
+        for (int64_t i = first; i < issued; ++i)
+          wait_bounded(smem_addr(&full[i % kStages]), static_cast<uint32_t>(i / kStages) & 1u, &no_abort, status,
+                       kStQuant, timeout_ns);
       }
     }
-    int64_t mu = m0;
-    int ku = kb0;
+  } else {
+    // ------------------------------------------------------------ consumers --
+    int64_t used = 0;
+    for (int64_t c = blockIdx.x; c < chunks; c += gridDim.x, ++used) {
+      const int st = static_cast<int>(used % kStages);
+      const uint32_t ph = static_cast<uint32_t>(used / kStages) & 1u;
+      const bool got = wait_bounded(smem_addr(&full[st]), ph, abort_flag, status, kStQuant, timeout_ns);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const int64_t m = c / per_row;
+      const int g0 = static_cast<int>(c - m * per_row) * kChunkGroups;
+      const int ng = KB - g0 < kChunkGroups ? KB - g0 : kChunkGroups;
+      // two groups per warp at a time (j and j + kConsumerWarps), interleaved
+      // so their dependent reduce / divide / convert chains overlap
+      for (int j = warp; j < ng; j += 2 * kConsumerWarps) {
+        const bool two = j + kConsumerWarps < ng;  // warp-uniform
+        float v[2][4];
+        lds4(ring + st * kChunkBytes + (j * kBlk + lane * 4) * static_cast<int>(sizeof(T)),
+             static_cast<const T*>(nullptr), v[0]);
+        if (two)
+          lds4(ring + st * kChunkBytes + ((j + kConsumerWarps) * kBlk + lane * 4) * static_cast<int>(sizeof(T)),
+               static_cast<const T*>(nullptr), v[1]);
+        float a[2];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (g0 + u >= g_end) break;  // warp-uniform
-      float v[4];
-      widen(raw[u], v);
-      float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        for (int u = 0; u < 2; ++u)
+          a[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-      const float scale = a > 0.0f ? a / kQmax : 1.0f;
-      *reinterpret_cast<uint32_t*>(xq + mu * ldq + ku * kBlk + lane * 4) = quant4(v, scale);
-      if (lane == 0) xs[mu * xs_sm + ku * xs_sk] = scale;
-      if (++ku == KB) {
-        ku = 0;
-        ++mu;
+        for (int o = 16; o > 0; o >>= 1) {
+          a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], o));
+          a[1] = fmaxf(a[1], __shfl_xor_sync(0xffffffffu, a[1], o));
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          if (u == 1 && !two) break;
+          const float scale = a[u] > 0.0f ? a[u] / kQmax : 1.0f;
+          const int64_t kb = g0 + j + u * kConsumerWarps;
+          *reinterpret_cast<uint32_t*>(xq + m * ldq + kb * kBlk + lane * 4) = quant4(v[u], scale);
+          if (lane == 0) xs[m * xs_sm + kb * xs_sk] = scale;
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&empty[st]));
     }
   }
+  __syncthreads();
 }
 
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -150,30 +185,37 @@ extern "C" int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, in
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return FACK_ERR_CUDA;
   if (major != 10 || minor != 0) return FACK_ERR_UNSUPPORTED_ARCH;
+  unsigned int* status = fack::device_status_word();
+  if (!status) return FACK_ERR_CUDA;
   const int KB = K / kBlk;
-  const int64_t groups = static_cast<int64_t>(M) * KB;
-  // one resident wave of the grid-stride loop (occupancy of the variant),
-  // never more warps than groups
-  static int resident[2] = {0, 0};
-  int& per_sm = resident[x_dtype];
-  if (per_sm == 0) {
-    const cudaError_t e =
-        x_dtype == FACK_DTYPE_F32
-            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quant_act_kernel<float>, kThreads, 0)
-            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quant_act_kernel<__nv_bfloat16>, kThreads, 0);
-    if (e != cudaSuccess || per_sm < 1) return FACK_ERR_CUDA;
-  }
-  const int64_t want = (groups + (kThreads / 32) * 8 - 1) / ((kThreads / 32) * 8);  // >= 8 groups per warp
-  const int64_t wave = static_cast<int64_t>(sms) * per_sm;
-  const int blocks = static_cast<int>(want < wave ? want : wave);
+  const int64_t chunks = static_cast<int64_t>(M) * ((KB + kChunkGroups - 1) / kChunkGroups);
+  // two persistent CTAs per SM (32 quantising warps), never more CTAs than chunks
+  const int blocks = static_cast<int>(chunks < 2 * sms ? chunks : 2 * sms);
+  const int smem_f32 = kStages * kChunkGroups * kBlk * 4, smem_bf16 = kStages * kChunkGroups * kBlk * 2;
+  const uint64_t tmo = 2000000000ull;  // 2 s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (x_dtype == FACK_DTYPE_F32)
-    quant_act_kernel<float><<<blocks, kThreads, 0, s>>>(static_cast<const float*>(x), ldx, M, KB,
-                                                         static_cast<uint8_t*>(xq), ldq, x_scale, xs_stride_m,
-                                                         xs_stride_kb);
-  else
-    quant_act_kernel<__nv_bfloat16><<<blocks, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, M, KB,
-                                                                 static_cast<uint8_t*>(xq), ldq, x_scale,
-                                                                 xs_stride_m, xs_stride_kb);
+  if (x_dtype == FACK_DTYPE_F32) {
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(quant_act_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_f32) !=
+          cudaSuccess)
+        return FACK_ERR_LAUNCH;
+      configured = true;
+    }
+    quant_act_kernel<float><<<blocks, kQThreads, smem_f32, s>>>(static_cast<const float*>(x), ldx, M, KB,
+                                                                 static_cast<uint8_t*>(xq), ldq, x_scale, xs_stride_m,
+                                                                 xs_stride_kb, status, tmo);
+  } else {
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(quant_act_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem_bf16) != cudaSuccess)
+        return FACK_ERR_LAUNCH;
+      configured = true;
+    }
+    quant_act_kernel<__nv_bfloat16><<<blocks, kQThreads, smem_bf16, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, M, KB, static_cast<uint8_t*>(xq), ldq, x_scale, xs_stride_m,
+        xs_stride_kb, status, tmo);
+  }
   return cudaGetLastError() == cudaSuccess ? FACK_OK : FACK_ERR_LAUNCH;
 }

@@ -63,3 +63,29 @@ def test_quant_feeds_gemm(cuda_device):
     err = (out.float().cpu() - ref.float()).abs()
     assert torch.isfinite(out.float()).all()
     assert bool((err <= 1e-2 + 1e-2 * ref.float().abs()).all())
+
+
+@pytest.mark.parametrize("s", [1.0, 3.0, 0.7, 1e-3, 5e4])
+def test_quant_rounding_midpoints(cuda_device, s):
+    """Values that scale onto e4m3 rounding midpoints (and within a few fp32
+    ulps of them), and around the subnormal boundary 2^-6: the codes must
+    equal the correctly rounded division's, whatever shortcut the kernel takes."""
+    mids = []
+    for e in range(-6, 8):                        # e4m3 normal binades up to 240
+        for mant in range(8):
+            lo = (1 + mant / 8) * 2.0 ** e
+            mids.append(lo + 2.0 ** e / 16)       # halfway to the next code
+    mids = torch.tensor([m for m in mids if m < 240], dtype=torch.float32)
+    vals = []
+    for k in range(-8, 9):                        # nudge by k fp32 ulps
+        vals.append(torch.nextafter(mids, torch.full_like(mids, float("inf") if k > 0 else 0.0)) if k else mids)
+        for _ in range(abs(k) - 1):
+            vals[-1] = torch.nextafter(vals[-1], torch.full_like(mids, float("inf") if k > 0 else 0.0))
+    v = torch.cat(vals + [torch.tensor([2.0 ** -6, 2.0 ** -6 * (1 - 2 ** -20), 2.0 ** -6 * (1 + 2 ** -20),
+                                        2.0 ** -7 * 1.5, 2.0 ** -9 * 0.5])])
+    n = (v.numel() + 126) // 127 * 127
+    v = torch.cat([v, torch.ones(n - v.numel())])
+    groups = v.view(-1, 127) * s
+    x = torch.cat([torch.full((groups.shape[0], 1), 240.0 * s), groups], dim=1)   # amax pins scale = s
+    x = torch.cat([x, -x], dim=0)
+    _check(x.to(cuda_device), "logical")
