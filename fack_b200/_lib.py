@@ -12,6 +12,14 @@ from pathlib import Path
 _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "libfack_gemm.so"
 
+# Exact-shape plan table shipped with the library (rows measured on B200 by
+# ``python -m fack_b200.tune``), loaded into the C table with the library.
+# More tables, separated by os.pathsep, are merged on top of it from this
+# variable, later rows replacing earlier ones -- the counterpart of aiter's
+# AITER_CONFIG_GEMM_A8W8_BLOCKSCALE_BPRESHUFFLE (client/aiter/dispatch.py:29-30).
+TUNED_TABLE = _HERE / "configs" / "a8w8_blockscale_bpreshuffle_tuned_gemm.csv"
+TUNED_ENV = "FACK_CONFIG_GEMM_A8W8_BLOCKSCALE_BPRESHUFFLE"
+
 # Status codes, mirrored from enum fack_status.
 FACK_OK = 0
 FACK_ERR_BAD_SHAPE = 1
@@ -52,6 +60,11 @@ SIGNATURES = {
     "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "fack_quant_act": (_c_int, [_c_p, _c_int, _c_i64, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p]),
     "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
+    "fack_gemm_bs_tuned_set": (_c_int, [_c_int] * 7),
+    "fack_gemm_bs_tuned_lookup": (_c_int, [_c_int] * 4 + [ctypes.POINTER(_c_int)] * 3),
+    "fack_gemm_bs_tuned_count": (_c_int, []),
+    "fack_gemm_bs_tuned_clear": (_c_int, []),
+    "fack_gemm_bs_tuned_load": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
 }
 
 _lib = None
@@ -74,7 +87,30 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
         fn.argtypes = args
     if path is None:
         _lib = lib
+        for table in tuned_tables():
+            load_tuned(table, lib)
     return lib
+
+
+def tuned_tables() -> list:
+    """The plan tables loaded with the library, in merge order."""
+    tables = [TUNED_TABLE] if TUNED_TABLE.exists() else []
+    extra = os.environ.get(TUNED_ENV, "")
+    return tables + [Path(p) for p in extra.split(os.pathsep) if p]
+
+
+def load_tuned(path: os.PathLike | str, lib: ctypes.CDLL | None = None) -> tuple:
+    """Merge a tuned-plan CSV into the library's table; returns (rows loaded,
+    rows skipped because they name another library's kernel).  Raises
+    ValueError naming the file and line of the first bad row (the table is
+    then unchanged)."""
+    lib = lib or load()
+    n, skipped = ctypes.c_int(), ctypes.c_int()
+    st = lib.fack_gemm_bs_tuned_load(os.fsencode(str(path)), ctypes.byref(n), ctypes.byref(skipped))
+    if st != FACK_OK:
+        raise ValueError(f"tuned table {path}: {lib.fack_status_string(st).decode()}: "
+                         f"{lib.fack_last_error().decode()}")
+    return n.value, skipped.value
 
 
 def status_string(code: int) -> str:

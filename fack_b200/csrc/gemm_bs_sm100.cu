@@ -46,6 +46,7 @@
 
 #include "../../include/fack_gemm.h"
 #include "sm100_ptx.cuh"
+#include "tuned_table.h"
 
 namespace fack {
 
@@ -675,6 +676,8 @@ static int fail(int status, const char* what, cudaError_t err = cudaSuccess) {
     snprintf(g_last_error, sizeof(g_last_error), "%s", what);
   return status;
 }
+int record_error(int status, const char* what) { return fail(status, what); }
+
 static DeviceInfo g_dev[kMaxDevices];
 static EncodeTiledFn g_encode = nullptr;
 
@@ -1017,8 +1020,11 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
     DeviceInfo* d = nullptr;
     const int st = device_info(&d);
     if (st != FACK_OK) return st;
-    const int st2 = plan_auto(d, M, N, K, tm, bn, &tm, &bn, &sp);
-    if (st2 != FACK_OK) return st2;
+    // an exact-shape row of the tuned table fixes a fully automatic plan
+    if (tm || bn || !tuned_lookup(d->sms, M, N, K, &tm, &bn, &sp)) {
+      const int st2 = plan_auto(d, M, N, K, tm, bn, &tm, &bn, &sp);
+      if (st2 != FACK_OK) return st2;
+    }
   }
   *tile_m = tm;
   *tile_n = bn;

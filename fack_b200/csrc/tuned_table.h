@@ -1,0 +1,22 @@
+// tuned_table.h -- internal interface of the exact-shape plan table
+// (tuned_table.cpp) used by the GEMM planner (gemm_bs_sm100.cu).
+#pragma once
+
+namespace fack {
+
+constexpr int kTunedMaxSplit = 8;  // the GEMM's cluster limit along K
+
+// Checks a fully specified plan against the kernel's rules: M >= 1, N and K
+// positive multiples of 128; tile_m 128 (one CTA) or 256 (a CTA pair);
+// tile_n 64, 128 or 256 dividing N; 1 <= split_k <= min(8, K/128), and
+// 2 * split_k <= 8 for a pair.  Returns a FACK_* status.
+int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k);
+
+// The row for (cu_num, M, N, K), if any.  Thread-safe.
+bool tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k);
+
+// Records `what` as the calling thread's fack_last_error text and returns
+// `status` (gemm_bs_sm100.cu).
+int record_error(int status, const char* what);
+
+}  // namespace fack

@@ -77,7 +77,9 @@ const char* fack_last_error(void);
  * library's choice -- and the workspace bytes fack_gemm_bs_ex needs for that
  * plan when the caller supplies a workspace (0 for a single K slice).  A
  * library choice of split-K queries the current device (cluster occupancy); an
- * explicit split does not.  Plays the role of aiter's per-shape
+ * explicit split does not.  When all three requests are 0, an exact-shape row
+ * of the tuned table (fack_gemm_bs_tuned_*) for the current device's SM count
+ * takes precedence over the cost model.  Plays the role of aiter's per-shape
  * kernelName/splitK selection (client/aiter/dispatch.py:142-150).
  */
 int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_request,
@@ -96,6 +98,34 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
  */
 int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
                         int* tile_n, int* split_k);
+
+/*
+ * Exact-shape plan table, the B200 counterpart of aiter's tuned GEMM CSV
+ * (rows keyed by cu_num, M, N, K with kernelName and splitK;
+ * client/aiter/dispatch.py:23-35, exact match only, dispatch.py:3-6).  Rows
+ * are keyed by (SM count, M, N, K) and fix tile_m, tile_n and split_k of the
+ * automatic plan for exactly that shape; other shapes keep the cost model.
+ * The table is process-wide and thread-safe.
+ *
+ * fack_gemm_bs_tuned_set: add or replace one row (BAD_SHAPE / BAD_ARG if the
+ *   plan is not valid for the shape, as for an explicit request).
+ * fack_gemm_bs_tuned_lookup: the row for a key, or 0, 0, 0 if there is none.
+ * fack_gemm_bs_tuned_count / _clear: number of rows / remove all rows.
+ * fack_gemm_bs_tuned_load: merge a CSV file.  '#' lines are comments, the
+ *   first other line is a header, columns are found by name: cu_num, M, N, K,
+ *   kernelName (fack_bs_sm100_t{128|256}x{64|128|256}_s{S}) are required,
+ *   splitK (= S) and errRatio (= 0) are checked when present.  Rows naming
+ *   another library's kernel are skipped and counted in *rows_skipped.  The
+ *   whole file is checked before any row is added; on a bad row the table is
+ *   unchanged, BAD_ARG is returned and fack_last_error gives "path:line: why".
+ *   A later row for the same key replaces an earlier one.
+ */
+int fack_gemm_bs_tuned_set(int cu_num, int M, int N, int K, int tile_m, int tile_n, int split_k);
+int fack_gemm_bs_tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n,
+                              int* split_k);
+int fack_gemm_bs_tuned_count(void);
+int fack_gemm_bs_tuned_clear(void);
+int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skipped);
 
 /*
  * Bytes of workspace fack_gemm_bs needs for this problem and split (0 when the
