@@ -82,6 +82,8 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
             "The FP8 block-scaled GEMM has no fallback implementation.")
     lib = ctypes.CDLL(str(p))
     for name, (res, args) in SIGNATURES.items():
+        if path is not None and not hasattr(lib, name):
+            continue  # another build (e.g. an older one under comparison) may predate this entry
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
