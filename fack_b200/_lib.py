@@ -39,6 +39,9 @@ FACK_W_PACKED = 1
 FACK_DTYPE_F32 = 0
 FACK_DTYPE_BF16 = 1
 
+FACK_GEMM_BF16 = 0
+FACK_GEMM_I8 = 1
+
 # Every symbol the header declares, with its ctypes signature.
 _c_int, _c_i64, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t
 SIGNATURES = {
@@ -60,6 +63,9 @@ SIGNATURES = {
     "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "fack_quant_act": (_c_int, [_c_p, _c_int, _c_i64, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p]),
     "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
+    "fack_gemm_tn_plan": (_c_int, [_c_int] * 6 + [ctypes.POINTER(_c_int)] * 2),
+    "fack_gemm_tn": (_c_int, [_c_int, _c_p, _c_i64, _c_p, _c_int, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64,
+                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_p]),
     "fack_gemm_bs_tuned_set": (_c_int, [_c_int] * 7),
     "fack_gemm_bs_tuned_lookup": (_c_int, [_c_int] * 4 + [ctypes.POINTER(_c_int)] * 3),
     "fack_gemm_bs_tuned_count": (_c_int, []),

@@ -18,8 +18,9 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libfack_gemm.so"
-SOURCES = [CSRC / "gemm_bs_sm100.cu", CSRC / "quant_act_sm100.cu", CSRC / "tuned_table.cpp"]
-HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "tuned_table.h", ROOT / "include" / "fack_gemm.h"]
+SOURCES = [CSRC / "gemm_bs_sm100.cu", CSRC / "gemm_tn_sm100.cu", CSRC / "quant_act_sm100.cu",
+           CSRC / "tuned_table.cpp"]
+HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "tuned_table.h", CSRC / "fack_internal.h", ROOT / "include" / "fack_gemm.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1184,6 +1184,21 @@ unsigned int* device_status_word() {
   void* p = nullptr;
   return cudaGetSymbolAddress(&p, g_status) == cudaSuccess ? static_cast<unsigned int*>(p) : nullptr;
 }
+
+int sm100_device(int* sms) {
+  DeviceInfo* d = nullptr;
+  const int st = device_info(&d);
+  if (st != FACK_OK) return st;
+  *sms = d->sms;
+  return FACK_OK;
+}
+
+int encode_bytes_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  return encode_2d(map, ptr, inner, outer, row_bytes, box_inner, box_outer,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+}
 }  // namespace fack
 
 extern "C" {

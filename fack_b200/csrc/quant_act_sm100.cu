@@ -26,11 +26,9 @@
 #include <stdint.h>
 
 #include "../../include/fack_gemm.h"
+#include "fack_internal.h"
 #include "sm100_ptx.cuh"
 
-namespace fack {
-unsigned int* device_status_word();  // gemm_bs_sm100.cu
-}
 
 namespace fack_quant {
 

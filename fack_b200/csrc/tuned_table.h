@@ -2,6 +2,8 @@
 // (tuned_table.cpp) used by the GEMM planner (gemm_bs_sm100.cu).
 #pragma once
 
+#include "fack_internal.h"
+
 namespace fack {
 
 constexpr int kTunedMaxSplit = 8;  // the GEMM's cluster limit along K
@@ -14,9 +16,5 @@ int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k);
 
 // The row for (cu_num, M, N, K), if any.  Thread-safe.
 bool tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k);
-
-// Records `what` as the calling thread's fack_last_error text and returns
-// `status` (gemm_bs_sm100.cu).
-int record_error(int status, const char* what);
 
 }  // namespace fack

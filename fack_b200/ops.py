@@ -285,28 +285,33 @@ def quantize_activations(x: torch.Tensor, layout: str = "aiter"):
 
 
 def shuffle_weight(b: torch.Tensor, layout=(16, 16)) -> torch.Tensor:
-    """Pre-pack an e4m3 ``[N, K]`` weight into this library's tile layout.
+    """Pre-pack a ``[N, K]`` weight into this library's tile layout.
 
     Stand-in for aiter's ``shuffle_weight(b, layout=(16, 16))``
-    (client/aiter/hsa/gfx942/driver.py:21).  The returned tensor has the same
-    shape and dtype, holds 128x128 tiles in their 128-byte-swizzled shared
-    memory image, and is marked ``is_shuffled = True``.  ``layout`` is
+    (client/aiter/hsa/gfx942/driver.py:21; gemm_driver.py:49, :67 for the
+    sibling families).  e4m3, bf16 and int8 weights are accepted: the layout
+    is defined on bytes -- 128-row x 128-byte tiles (128 e4m3 / int8 or 64
+    bf16 elements of K) in their 128-byte-swizzled shared-memory image -- so
+    N % 128 == 0 and K x element size % 128 == 0.  The returned tensor has the
+    same shape and dtype and is marked ``is_shuffled = True``.  ``layout`` is
     accepted for signature compatibility; the only supported value is
     ``(16, 16)``.
     """
     if tuple(layout) != (16, 16):
         raise ValueError("only layout=(16, 16) is supported")
-    if not isinstance(b, torch.Tensor) or not b.is_cuda or b.dtype != FP8 or b.dim() != 2:
-        raise ValueError("shuffle_weight needs a 2-D float8_e4m3fn CUDA tensor")
+    if not isinstance(b, torch.Tensor) or not b.is_cuda or b.dim() != 2 or \
+            b.dtype not in (FP8, torch.bfloat16, torch.int8):
+        raise ValueError("shuffle_weight needs a 2-D float8_e4m3fn, bfloat16 or int8 CUDA tensor")
     N, K = b.shape
-    if N % BLOCK or K % BLOCK:
-        raise ValueError("shuffle_weight requires N%128 == K%128 == 0")
+    es = b.element_size()
+    if N % BLOCK or (K * es) % BLOCK:
+        raise ValueError("shuffle_weight requires N % 128 == 0 and K x element size % 128 == 0")
     if b.stride(1) != 1:
         raise ValueError("weight rows must be contiguous")
-    packed = torch.empty((N, K), dtype=FP8, device=b.device)
+    packed = torch.empty((N, K), dtype=b.dtype, device=b.device)
     lib = _lib.load()
     with torch.cuda.device(b.device):
-        st = lib.fack_gemm_bs_prepack_w(b.data_ptr(), b.stride(0), None, N, K, packed.data_ptr(), None,
+        st = lib.fack_gemm_bs_prepack_w(b.data_ptr(), b.stride(0) * es, None, N, K * es, packed.data_ptr(), None,
                                         _stream_handle(b.device))
     _lib.check(st, "fack_gemm_bs_prepack_w")
     packed.is_shuffled = True

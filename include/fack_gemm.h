@@ -53,6 +53,12 @@ enum fack_w_layout {
   FACK_W_PACKED = 1      /* output of fack_gemm_bs_prepack_w                   */
 };
 
+/* Sibling GEMM families of fack_gemm_tn (argument `kind`). */
+enum fack_gemm_kind {
+  FACK_GEMM_BF16 = 0,    /* bf16 A, B; fp32 accumulation                        */
+  FACK_GEMM_I8 = 1       /* int8 A, B; s32 accumulation, per-row/column scales  */
+};
+
 /* Element types of the activation input to fack_quant_act (argument `x_dtype`). */
 enum fack_dtype {
   FACK_DTYPE_F32 = 0,    /* fp32                                               */
@@ -250,6 +256,35 @@ int fack_gather_interleave(const void* gathered, int g, int M, int n_shard,
  */
 int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, int K, void* xq, int64_t ldq,
                    float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb, void* stream);
+
+/*
+ * The sibling GEMM families the reference drives through the same client
+ * (client/aiter/hsa/gfx942/gemm_driver.py:32-79), both "TN" (A[M,K] and
+ * B[N,K] row-major, K contiguous), bf16 output Y[M,N] with row stride ldo:
+ *
+ *   kind = FACK_GEMM_BF16: Y = bf16(A . B^T (+ bias)), A and B bf16, fp32
+ *     accumulation; a_scale and b_scale must be NULL (gemm_driver.py:47-48,
+ *     aiter's gemm_a16w16_asm).
+ *   kind = FACK_GEMM_I8: Y = bf16((float(A . B^T) * a_scale[m]) * b_scale[n]
+ *     (+ bias[n])), A and B int8, exact s32 accumulation, each product and
+ *     the sum rounded in fp32 in that order (gemm_driver.py:58-68, aiter's
+ *     gemm_a8w8_asm with per-token scales and an fp32 bias).
+ *
+ * lda / ldb / ldo are in elements; A and B rows 16-byte aligned (lda, ldb
+ * times the element size a multiple of 16; the reference pads int8 rows to
+ * K + 128); ldo % 8 == 0.  K x element size % 128 == 0 (bf16: K % 64, int8:
+ * K % 128); N % 64 == 0; 1 <= M <= 8388480.  b_packed = 1 takes B from
+ * fack_gemm_bs_prepack_w applied to B's bytes (N rows of K x element size
+ * bytes; ldb is then ignored).  bias is optional (NULL).  tile_n (64, 128,
+ * 256) and split_k (1..8) 0 = the library's choice (fack_gemm_tn_plan, which
+ * queries the current device unless both are given).  Capturable; allocates
+ * nothing.
+ */
+int fack_gemm_tn_plan(int kind, int M, int N, int K, int tile_n_request, int split_k_request, int* tile_n,
+                      int* split_k);
+int fack_gemm_tn(int kind, const void* a, int64_t lda, const void* b, int b_packed, int64_t ldb,
+                 const float* a_scale, const float* b_scale, const float* bias, void* out, int64_t ldo, int M,
+                 int N, int K, int tile_n, int split_k, void* stream);
 
 /*
  * Reads (and with reset != 0 clears) the current device's error word, which a

@@ -116,6 +116,40 @@ def test_pointer_and_stride_checks_before_device():
     assert lib.fack_quant_act(ok, f32, K, M, K, ok, K + 8, ok, 1, M, None) == _lib.FACK_ERR_BAD_STRIDE
 
 
+def test_sibling_gemm_validation_before_device():
+    lib = _lib.load()
+    ok = 1 << 20
+    BF, I8 = _lib.FACK_GEMM_BF16, _lib.FACK_GEMM_I8
+    M, N, K = 32, 256, 256
+
+    def tn(kind=I8, a=ok, lda=K, b=ok, packed=0, ldb=K, sa=ok, sb=ok, bias=None, out=ok, ldo=N, m=M, n=N, k=K,
+           tile=0, split=1):
+        return lib.fack_gemm_tn(kind, a, lda, b, packed, ldb, sa, sb, bias, out, ldo, m, n, k, tile, split, None)
+
+    assert tn(kind=2) == _lib.FACK_ERR_BAD_ARG
+    assert tn(n=192 + 32) == _lib.FACK_ERR_BAD_SHAPE            # N % 64
+    assert tn(k=192) == _lib.FACK_ERR_BAD_SHAPE                 # int8: K % 128
+    assert tn(kind=BF, sa=None, sb=None, k=96, lda=96, ldb=96) == _lib.FACK_ERR_BAD_SHAPE
+    assert tn(m=0) == _lib.FACK_ERR_BAD_SHAPE
+    assert tn(a=ok + 8) == _lib.FACK_ERR_BAD_ALIGN
+    assert tn(sa=None) == _lib.FACK_ERR_BAD_ALIGN               # int8 needs both scale vectors
+    assert tn(bias=ok + 2) == _lib.FACK_ERR_BAD_ALIGN
+    assert tn(kind=BF) == _lib.FACK_ERR_BAD_ARG                 # bf16 takes no scales
+    assert tn(lda=K + 8) == _lib.FACK_ERR_BAD_STRIDE            # int8 rows: 16-byte multiple
+    assert tn(kind=BF, sa=None, sb=None, lda=K + 4) == _lib.FACK_ERR_BAD_STRIDE
+    assert tn(ldo=N + 4) == _lib.FACK_ERR_BAD_STRIDE
+    assert tn(packed=2) == _lib.FACK_ERR_BAD_ARG
+    assert tn(split=9) == _lib.FACK_ERR_BAD_ARG
+    assert tn(tile=96) == _lib.FACK_ERR_BAD_ARG
+    tn_, sk = ctypes.c_int(), ctypes.c_int()
+    # a fully explicit plan needs no device
+    assert lib.fack_gemm_tn_plan(I8, M, N, K, 128, 2, ctypes.byref(tn_), ctypes.byref(sk)) == 0
+    assert (tn_.value, sk.value) == (128, 2)
+    assert lib.fack_gemm_tn_plan(I8, M, 320, K, 256, 1, ctypes.byref(tn_), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_tn_plan(BF, M, N, 128, 64, 3, ctypes.byref(tn_), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_tn_plan(BF, M, N, 192, 64, 3, ctypes.byref(tn_), ctypes.byref(sk)) == 0  # bf16: K % 64
+
+
 def test_check_maps_contract_violations_to_valueerror():
     with pytest.raises(ValueError):
         _lib.check(_lib.FACK_ERR_BAD_SHAPE, "x")
