@@ -1,6 +1,6 @@
 """Paired A/B comparison of two versions of the GEMM on B200.
 
-``python -m fack_b200.abtest BASELINE CANDIDATE --shape M,N,K [--shape ...]
+``python -m fack_b200.abtest <baseline> <candidate> --shape M,N,K [--shape ...]
 --pairs 8 --min-gain 0.01 --alpha 0.05``
 
 A version is either a build of the library (a path to a ``libfack_gemm.so``)

@@ -71,8 +71,8 @@ QMAX = 240.0
 def quantize_activations_ref(x: torch.Tensor):
     """(XQ e4m3 [M,K], logical x_scale fp32 [M,K/128]) from fp32 or bf16 X.
 
-    The activation construction of the benchmark configs (BASELINE's
-    "quantised per row per 128-K group with x_scale = amax/240"): per token
+    The activation construction of the benchmark workloads ("quantised per
+    row per 128-K group with x_scale = amax/240"): per token
     and 128-wide K group, scale = amax(|x|)/240 (1 for an all-zero group),
     code = e4m3fn(clamp(x/scale, -240, 240)) rounded to nearest even; bf16
     input is widened to fp32 first.  The reference takes X already quantised
