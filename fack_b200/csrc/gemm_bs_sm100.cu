@@ -43,6 +43,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/fack_gemm.h"
 #include "sm100_ptx.cuh"
@@ -54,7 +55,6 @@ constexpr int kBlk = 128;          // quantisation block along K and N
 constexpr int kTileM = 128;        // tokens per CTA (UMMA M, TMEM lanes)
 constexpr int kThreads = 384;      // 12 warps = 3 warpgroups
 constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..11 rescale and store
-constexpr int kEpiWarps = 8;
 constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
 constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kGroupM = 16;        // token-tile band of the grouped launch order
@@ -92,6 +92,9 @@ struct Cfg {
   static constexpr int kCpw = BN / 2;                       // columns per rescale warp
   static constexpr int kPitch32 = BN + 4;                   // fp32 staging pitch (floats)
   static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
+  // paired fp32 FMA (fma.rn.f32x2) in the rescale: half the instructions; the
+  // 128-wide tiles keep scalar FMAs, with which their registers fit unspilled
+  static constexpr bool kPairedFma = BN != 128;
   // shared-memory carve-up (offsets from a 1024-byte aligned base); both CTAs
   // of a pair use identical offsets, which the pair MMA relies on
   static constexpr int kOffA = 0;
@@ -407,9 +410,20 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // where this warp reports a released TMEM buffer: the MMA issuer's CTA
     const uint32_t tempty_base = PAIR ? dsmem_map(bar_tempty(0), leader_rank) : bar_tempty(0);
     if (q < quarters) {
-      float acc[C::kCpw];
+      // fp32 accumulators: two per 64-bit register where the rescale uses the
+      // paired FMA (its operand form), else one float each
+      constexpr int kAccN = C::kPairedFma ? C::kCpw / 2 : C::kCpw;
+      using AccT = typename std::conditional<C::kPairedFma, uint64_t, float>::type;
+      AccT acc[kAccN];
 #pragma unroll
-      for (int j = 0; j < C::kCpw; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < kAccN; ++j) acc[j] = AccT(0);
+      // columns j, j+1 (j even) of the accumulator
+      auto acc_pair = [&](int j) -> float2 {
+        if constexpr (C::kPairedFma)
+          return unpack_f32x2(acc[j >> 1]);
+        else
+          return make_float2(acc[j], acc[j + 1]);
+      };
       // Scales: x_scale[m0+tok, kb] and w_scale[block of this column half, kb]
       // prefetched kPrefetch K blocks ahead with cp.async into this thread's
       // private shared slots (one commit group per K block).
@@ -438,6 +452,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const uint32_t bph = (i / C::kTmemBufs) & 1;
         cp_async_wait<kPrefetch - 1>();  // this thread's copies for K block i have landed
         const float sc = raw_xp[(i % kPrefetch) * 256] * raw_wp[(i % kPrefetch) * 256];
+        const uint64_t sc2 = C::kPairedFma ? pack_f32x2(sc, sc) : 0ull;
         prefetch(i + kPrefetch);
         // tcgen05.ld is .sync.aligned: the whole warp must agree before using it.
         const bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
@@ -458,12 +473,24 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           if ((c & 1) == 0) {
             if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, vb);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) acc[c * 32 + t] = fmaf(__uint_as_float(va[t]), sc, acc[c * 32 + t]);
+            for (int t = 0; t < 32; t += 2)
+              if constexpr (C::kPairedFma) {
+                fma2_acc(acc[(c * 32 + t) >> 1], va[t], va[t + 1], sc2);
+              } else {
+                acc[c * 32 + t] = fmaf(__uint_as_float(va[t]), sc, acc[c * 32 + t]);
+                acc[c * 32 + t + 1] = fmaf(__uint_as_float(va[t + 1]), sc, acc[c * 32 + t + 1]);
+              }
             if (c + 1 < kChunks) tmem_wait32(vb);
           } else {
             if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, va);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) acc[c * 32 + t] = fmaf(__uint_as_float(vb[t]), sc, acc[c * 32 + t]);
+            for (int t = 0; t < 32; t += 2)
+              if constexpr (C::kPairedFma) {
+                fma2_acc(acc[(c * 32 + t) >> 1], vb[t], vb[t + 1], sc2);
+              } else {
+                acc[c * 32 + t] = fmaf(__uint_as_float(vb[t]), sc, acc[c * 32 + t]);
+                acc[c * 32 + t + 1] = fmaf(__uint_as_float(vb[t + 1]), sc, acc[c * 32 + t + 1]);
+              }
             if (c + 1 < kChunks) tmem_wait32(va);
           }
         }
@@ -484,17 +511,21 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         if (S > 1) {
           float* row = reinterpret_cast<float*>(smem + C::kOffA) + tok * C::kPitch32 + col0;
 #pragma unroll
-          for (int j = 0; j < C::kCpw; j += 4)
-            *reinterpret_cast<float4*>(row + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+          for (int j = 0; j < C::kCpw; j += 4) {
+            const float2 lo = acc_pair(j), hi = acc_pair(j + 2);
+            *reinterpret_cast<float4*>(row + j) = make_float4(lo.x, lo.y, hi.x, hi.y);
+          }
         } else {
           __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffA) + tok * C::kPitch16 + col0;
 #pragma unroll
           for (int j = 0; j < C::kCpw; j += 8) {
             uint4 v;
-            __nv_bfloat162 b0 = __floats2bfloat162_rn(acc[j + 0], acc[j + 1]);
-            __nv_bfloat162 b1 = __floats2bfloat162_rn(acc[j + 2], acc[j + 3]);
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[j + 4], acc[j + 5]);
-            __nv_bfloat162 b3 = __floats2bfloat162_rn(acc[j + 6], acc[j + 7]);
+            const float2 f0 = acc_pair(j), f1 = acc_pair(j + 2);
+            const float2 f2 = acc_pair(j + 4), f3 = acc_pair(j + 6);
+            __nv_bfloat162 b0 = __floats2bfloat162_rn(f0.x, f0.y);
+            __nv_bfloat162 b1 = __floats2bfloat162_rn(f1.x, f1.y);
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(f2.x, f2.y);
+            __nv_bfloat162 b3 = __floats2bfloat162_rn(f3.x, f3.y);
             v.x = *reinterpret_cast<uint32_t*>(&b0);
             v.y = *reinterpret_cast<uint32_t*>(&b1);
             v.z = *reinterpret_cast<uint32_t*>(&b2);

@@ -298,6 +298,29 @@ __device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// Two fp32 values packed in one 64-bit register (low word first), the operand
+// form of the sm_100 paired fp32 instructions.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 unpack_f32x2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
+// acc (two fp32) += (p0, p1) * s2 (two fp32) in one instruction; each lane is
+// an fp32 fused multiply-add rounded to nearest even, exactly as fmaf.
+__device__ __forceinline__ void fma2_acc(uint64_t& acc, uint32_t p0, uint32_t p1, uint64_t s2) {
+  asm("{\n\t.reg .b64 pa;\n\t"
+      "mov.b64 pa, {%1, %2};\n\t"
+      "fma.rn.f32x2 %0, pa, %3, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(p0), "r"(p1), "l"(s2));
+}
+
 // ------------------------------------------------------------- cp.async --
 // 4-byte asynchronous global->shared copy; src_bytes = 0 writes a zero.
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
