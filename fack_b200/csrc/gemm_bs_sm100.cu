@@ -94,7 +94,9 @@ struct Cfg {
   static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
   // paired fp32 FMA (fma.rn.f32x2) in the rescale: half the instructions; the
   // 128-wide tiles keep scalar FMAs, with which their registers fit unspilled
+  // (with paired FMAs they spill, whether TMEM is read 16 or 32 columns at a time)
   static constexpr bool kPairedFma = BN != 128;
+  static constexpr int kLdCols = 32;  // columns per double-buffered TMEM load
   // shared-memory carve-up (offsets from a 1024-byte aligned base); both CTAs
   // of a pair use identical offsets, which the pair MMA relies on
   static constexpr int kOffA = 0;
@@ -462,36 +464,40 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + col0;
-        // Double-buffered 32-column TMEM loads: chunk c+1 is in flight while
+        // Double-buffered kLd-column TMEM loads: chunk c+1 is in flight while
         // chunk c is folded into the accumulators.
-        constexpr int kChunks = C::kCpw / 32;
-        uint32_t va[32], vb[32];
-        tmem_ld32_nowait(taddr, va);
-        tmem_wait32(va);
+        constexpr int kLd = C::kLdCols;
+        constexpr int kChunks = C::kCpw / kLd;
+        auto ld_issue = [&](uint32_t addr, uint32_t(&v)[kLd]) {
+          if constexpr (kLd == 32) tmem_ld32_nowait(addr, v); else tmem_ld16_nowait(addr, v);
+        };
+        auto ld_wait = [&](uint32_t(&v)[kLd]) {
+          if constexpr (kLd == 32) tmem_wait32(v); else tmem_wait16(v);
+        };
+        auto fold = [&](int c, const uint32_t(&v)[kLd]) {
+#pragma unroll
+          for (int t = 0; t < kLd; t += 2) {
+            if constexpr (C::kPairedFma) {
+              fma2_acc(acc[(c * kLd + t) >> 1], v[t], v[t + 1], sc2);
+            } else {
+              acc[c * kLd + t] = fmaf(__uint_as_float(v[t]), sc, acc[c * kLd + t]);
+              acc[c * kLd + t + 1] = fmaf(__uint_as_float(v[t + 1]), sc, acc[c * kLd + t + 1]);
+            }
+          }
+        };
+        uint32_t va[kLd], vb[kLd];
+        ld_issue(taddr, va);
+        ld_wait(va);
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
           if ((c & 1) == 0) {
-            if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, vb);
-#pragma unroll
-            for (int t = 0; t < 32; t += 2)
-              if constexpr (C::kPairedFma) {
-                fma2_acc(acc[(c * 32 + t) >> 1], va[t], va[t + 1], sc2);
-              } else {
-                acc[c * 32 + t] = fmaf(__uint_as_float(va[t]), sc, acc[c * 32 + t]);
-                acc[c * 32 + t + 1] = fmaf(__uint_as_float(va[t + 1]), sc, acc[c * 32 + t + 1]);
-              }
-            if (c + 1 < kChunks) tmem_wait32(vb);
+            if (c + 1 < kChunks) ld_issue(taddr + (c + 1) * kLd, vb);
+            fold(c, va);
+            if (c + 1 < kChunks) ld_wait(vb);
           } else {
-            if (c + 1 < kChunks) tmem_ld32_nowait(taddr + (c + 1) * 32, va);
-#pragma unroll
-            for (int t = 0; t < 32; t += 2)
-              if constexpr (C::kPairedFma) {
-                fma2_acc(acc[(c * 32 + t) >> 1], vb[t], vb[t + 1], sc2);
-              } else {
-                acc[c * 32 + t] = fmaf(__uint_as_float(vb[t]), sc, acc[c * 32 + t]);
-                acc[c * 32 + t + 1] = fmaf(__uint_as_float(vb[t + 1]), sc, acc[c * 32 + t + 1]);
-              }
-            if (c + 1 < kChunks) tmem_wait32(va);
+            if (c + 1 < kChunks) ld_issue(taddr + (c + 1) * kLd, va);
+            fold(c, vb);
+            if (c + 1 < kChunks) ld_wait(va);
           }
         }
         tc_fence_before();
