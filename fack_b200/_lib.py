@@ -63,9 +63,9 @@ SIGNATURES = {
     "fack_gather_interleave": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_i64, _c_p]),
     "fack_quant_act": (_c_int, [_c_p, _c_int, _c_i64, _c_int, _c_int, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_p]),
     "fack_device_status": (_c_int, [_c_p, ctypes.POINTER(ctypes.c_uint), _c_int]),
-    "fack_gemm_tn_plan": (_c_int, [_c_int] * 6 + [ctypes.POINTER(_c_int)] * 2),
+    "fack_gemm_tn_plan": (_c_int, [_c_int] * 7 + [ctypes.POINTER(_c_int)] * 3),
     "fack_gemm_tn": (_c_int, [_c_int, _c_p, _c_i64, _c_p, _c_int, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64,
-                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_p]),
+                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p]),
     "fack_gemm_bs_tuned_set": (_c_int, [_c_int] * 7),
     "fack_gemm_bs_tuned_lookup": (_c_int, [_c_int] * 4 + [ctypes.POINTER(_c_int)] * 3),
     "fack_gemm_bs_tuned_count": (_c_int, []),

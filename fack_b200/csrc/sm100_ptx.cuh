@@ -321,6 +321,28 @@ __device__ __forceinline__ void fma2_acc(uint64_t& acc, uint32_t p0, uint32_t p1
       : "r"(p0), "r"(p1), "l"(s2));
 }
 
+// Pair forms (cta_group::2, M = 256: 128 rows in each CTA of the pair; the
+// leader issues, each CTA supplies half of the B rows from its own shared
+// memory and receives its 128 accumulator rows in its own TMEM).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_s8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // ------------------------------------------------------------- cp.async --
 // 4-byte asynchronous global->shared copy; src_bytes = 0 writes a zero.
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {

@@ -13,7 +13,8 @@ block-scaled FP8 path (client/aiter/hsa/gfx942/gemm_driver.py:32-79):
 Both take ``b`` either row-major or from :func:`fack_b200.shuffle_weight`
 (``bpreshuffle`` must say which, as in aiter).  ``kernelName`` may be one of
 the reference's gfx942 symbols (the library then picks its own tile) or this
-library's ``fack_tn_sm100_{bf16|i8}_t128x{64|128|256}_s{S}``.  ``splitK``
+library's ``fack_tn_sm100_{bf16|i8}_t{128|256}x{64|128|256}_s{S}`` (token tile
+256 = a pair of CTAs sharing each MMA; S <= 4 then).  ``splitK``
 None lets the library choose; an explicit value is honoured.  Contract
 violations raise ``ValueError`` before any launch.
 """
@@ -37,31 +38,33 @@ def _family(kind: int) -> str:
     return "bf16" if kind == _lib.FACK_GEMM_BF16 else "i8"
 
 
-def kernel_name(kind: int, tile_n: int, split_k: int) -> str:
-    return f"{PREFIX}_{_family(kind)}_t128x{tile_n}_s{split_k}"
+def kernel_name(kind: int, tile_m: int, tile_n: int, split_k: int) -> str:
+    return f"{PREFIX}_{_family(kind)}_t{tile_m}x{tile_n}_s{split_k}"
 
 
 def parse_kernel_name(kind: int, name) -> tuple:
-    """(tile_n, split_k) fixed by a kernel name, (0, 0) for the library's choice."""
+    """(tile_m, tile_n, split_k) fixed by a kernel name, (0, 0, 0) for the library's choice."""
     if not name or AITER_PATTERNS[kind] in str(name):
-        return 0, 0
-    m = re.fullmatch(PREFIX + r"_(bf16|i8)_t128x(64|128|256)_s([1-8])", str(name))
-    if not m or m.group(1) != _family(kind):
+        return 0, 0, 0
+    m = re.fullmatch(PREFIX + r"_(bf16|i8)_t(128|256)x(64|128|256)_s([1-8])", str(name))
+    if not m or m.group(1) != _family(kind) or (m.group(2) == "256" and int(m.group(4)) > 4):
         raise ValueError(f"unknown {_family(kind)} kernel {name!r}")
-    return int(m.group(2)), int(m.group(3))
+    return int(m.group(2)), int(m.group(3)), int(m.group(4))
 
 
-def plan(kind: int, M: int, N: int, K: int, tile_n: int = 0, split_k: int = 0) -> tuple:
+def plan(kind: int, M: int, N: int, K: int, tile_m: int = 0, tile_n: int = 0, split_k: int = 0) -> tuple:
+    """(tile_m, tile_n, split_k) the library uses; 0 = library choice."""
     lib = _lib.load()
-    tn, sk = ctypes.c_int(), ctypes.c_int()
-    _lib.check(lib.fack_gemm_tn_plan(kind, M, N, K, tile_n, split_k, ctypes.byref(tn), ctypes.byref(sk)),
-               "fack_gemm_tn_plan")
-    return tn.value, sk.value
+    tm, tn, sk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.check(lib.fack_gemm_tn_plan(kind, M, N, K, tile_m, tile_n, split_k, ctypes.byref(tm), ctypes.byref(tn),
+                                     ctypes.byref(sk)), "fack_gemm_tn_plan")
+    return tm.value, tn.value, sk.value
 
 
 def get_config(kind: int, M: int, N: int, K: int) -> dict:
-    tn, sk = plan(kind, M, N, K)
-    return {"libtype": "asm", "kernelName": kernel_name(kind, tn, sk), "splitK": sk, "tile_n": tn}
+    tm, tn, sk = plan(kind, M, N, K)
+    return {"libtype": "asm", "kernelName": kernel_name(kind, tm, tn, sk), "splitK": sk, "tile_m": tm,
+            "tile_n": tn}
 
 
 def _vec(t: Optional[torch.Tensor], n: int, name: str, dev) -> Optional[torch.Tensor]:
@@ -76,7 +79,7 @@ def _vec(t: Optional[torch.Tensor], n: int, name: str, dev) -> Optional[torch.Te
 def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
             a_scale: Optional[torch.Tensor] = None, b_scale: Optional[torch.Tensor] = None,
             bias: Optional[torch.Tensor] = None, packed: Optional[bool] = None, tile_n: int = 0,
-            split_k: int = 0) -> torch.Tensor:
+            split_k: int = 0, tile_m: int = 0) -> torch.Tensor:
     """Native entry: Y[M, N] bf16 from A[M, K] and B[N, K] (bf16, or int8 with
     a_scale [M] / b_scale [N]); ``packed`` defaults to ``b.is_shuffled``."""
     for nm, t in (("a", a), ("b", b)):
@@ -109,7 +112,7 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None
     with torch.cuda.device(dev):
         st = lib.fack_gemm_tn(kind, a.data_ptr(), a.stride(0), b.data_ptr(), int(packed), b.stride(0),
                               ptr(a_scale), ptr(b_scale), ptr(bias), out.data_ptr(), out.stride(0), M, N, K,
-                              int(tile_n), int(split_k), torch.cuda.current_stream(dev).cuda_stream)
+                              int(tile_m), int(tile_n), int(split_k), torch.cuda.current_stream(dev).cuda_stream)
     _lib.check(st, "fack_gemm_tn")
     return out
 
@@ -126,11 +129,11 @@ def gemm_a16w16_asm(a, b, out, bias=None, splitK=None, kernelName=None, bpreshuf
     """Drop-in for aiter's ``gemm_a16w16_asm`` (BF16 TN; writes and returns ``out``)."""
     if a.dtype != torch.bfloat16:
         raise ValueError("gemm_a16w16_asm takes bfloat16 operands")
-    tile_n, name_split = parse_kernel_name(_lib.FACK_GEMM_BF16, kernelName)
+    tile_m, tile_n, name_split = parse_kernel_name(_lib.FACK_GEMM_BF16, kernelName)
     shuffled = _check_shuffle_flag(b, bpreshuffle)
     split = name_split if splitK is None else int(splitK)
     return gemm_tn(a, b, out, bias=None if bias is None else bias.reshape(-1), packed=shuffled, tile_n=tile_n,
-                   split_k=split)
+                   split_k=split, tile_m=tile_m)
 
 
 def gemm_a8w8_asm(a, b, sa, sb, out, kernelName=None, bias=None, bpreshuffle=True, splitK=None):
@@ -138,9 +141,9 @@ def gemm_a8w8_asm(a, b, sa, sb, out, kernelName=None, bias=None, bpreshuffle=Tru
     writes and returns ``out``)."""
     if a.dtype != torch.int8:
         raise ValueError("gemm_a8w8_asm takes int8 operands")
-    tile_n, name_split = parse_kernel_name(_lib.FACK_GEMM_I8, kernelName)
+    tile_m, tile_n, name_split = parse_kernel_name(_lib.FACK_GEMM_I8, kernelName)
     shuffled = _check_shuffle_flag(b, bpreshuffle)
     split = name_split if splitK is None else int(splitK)
     flat = lambda t: None if t is None else t.reshape(-1)  # noqa: E731  ([M,1] / [N,1] / [1,N] views)
     return gemm_tn(a, b, out, a_scale=flat(sa), b_scale=flat(sb), bias=flat(bias), packed=shuffled,
-                   tile_n=tile_n, split_k=split)
+                   tile_n=tile_n, split_k=split, tile_m=tile_m)

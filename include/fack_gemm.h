@@ -275,16 +275,17 @@ int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, int K, void* 
  * K + 128); ldo % 8 == 0.  K x element size % 128 == 0 (bf16: K % 64, int8:
  * K % 128); N % 64 == 0; 1 <= M <= 8388480.  b_packed = 1 takes B from
  * fack_gemm_bs_prepack_w applied to B's bytes (N rows of K x element size
- * bytes; ldb is then ignored).  bias is optional (NULL).  tile_n (64, 128,
- * 256) and split_k (1..8) 0 = the library's choice (fack_gemm_tn_plan, which
- * queries the current device unless both are given).  Capturable; allocates
- * nothing.
+ * bytes; ldb is then ignored).  bias is optional (NULL).  tile_m (128 = one
+ * CTA per 128-row tile, 256 = a pair of CTAs sharing each MMA through
+ * cta_group::2), tile_n (64, 128, 256) and split_k (1..8; 2 x split <= 8 for
+ * pairs): 0 = the library's choice (fack_gemm_tn_plan, which queries the
+ * current device unless all three are given).  Capturable; allocates nothing.
  */
-int fack_gemm_tn_plan(int kind, int M, int N, int K, int tile_n_request, int split_k_request, int* tile_n,
-                      int* split_k);
+int fack_gemm_tn_plan(int kind, int M, int N, int K, int tile_m_request, int tile_n_request, int split_k_request,
+                      int* tile_m, int* tile_n, int* split_k);
 int fack_gemm_tn(int kind, const void* a, int64_t lda, const void* b, int b_packed, int64_t ldb,
                  const float* a_scale, const float* b_scale, const float* bias, void* out, int64_t ldo, int M,
-                 int N, int K, int tile_n, int split_k, void* stream);
+                 int N, int K, int tile_m, int tile_n, int split_k, void* stream);
 
 /*
  * Reads (and with reset != 0 clears) the current device's error word, which a

@@ -123,8 +123,8 @@ def test_sibling_gemm_validation_before_device():
     M, N, K = 32, 256, 256
 
     def tn(kind=I8, a=ok, lda=K, b=ok, packed=0, ldb=K, sa=ok, sb=ok, bias=None, out=ok, ldo=N, m=M, n=N, k=K,
-           tile=0, split=1):
-        return lib.fack_gemm_tn(kind, a, lda, b, packed, ldb, sa, sb, bias, out, ldo, m, n, k, tile, split, None)
+           tm=0, tile=0, split=1):
+        return lib.fack_gemm_tn(kind, a, lda, b, packed, ldb, sa, sb, bias, out, ldo, m, n, k, tm, tile, split, None)
 
     assert tn(kind=2) == _lib.FACK_ERR_BAD_ARG
     assert tn(n=192 + 32) == _lib.FACK_ERR_BAD_SHAPE            # N % 64
@@ -141,13 +141,21 @@ def test_sibling_gemm_validation_before_device():
     assert tn(packed=2) == _lib.FACK_ERR_BAD_ARG
     assert tn(split=9) == _lib.FACK_ERR_BAD_ARG
     assert tn(tile=96) == _lib.FACK_ERR_BAD_ARG
-    tn_, sk = ctypes.c_int(), ctypes.c_int()
+    assert tn(tm=192) == _lib.FACK_ERR_BAD_ARG
+    assert tn(tm=256, split=5) == _lib.FACK_ERR_BAD_ARG        # a pair's cluster is 2 x split <= 8
+    tm_, tn_, sk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+
+    def plan(kind, m, n, k, t_m, t_n, s):
+        st = lib.fack_gemm_tn_plan(kind, m, n, k, t_m, t_n, s, ctypes.byref(tm_), ctypes.byref(tn_), ctypes.byref(sk))
+        return st, (tm_.value, tn_.value, sk.value)
+
     # a fully explicit plan needs no device
-    assert lib.fack_gemm_tn_plan(I8, M, N, K, 128, 2, ctypes.byref(tn_), ctypes.byref(sk)) == 0
-    assert (tn_.value, sk.value) == (128, 2)
-    assert lib.fack_gemm_tn_plan(I8, M, 320, K, 256, 1, ctypes.byref(tn_), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
-    assert lib.fack_gemm_tn_plan(BF, M, N, 128, 64, 3, ctypes.byref(tn_), ctypes.byref(sk)) == _lib.FACK_ERR_BAD_ARG
-    assert lib.fack_gemm_tn_plan(BF, M, N, 192, 64, 3, ctypes.byref(tn_), ctypes.byref(sk)) == 0  # bf16: K % 64
+    assert plan(I8, M, N, K, 128, 128, 2) == (0, (128, 128, 2))
+    assert plan(I8, M, N, K, 256, 64, 2) == (0, (256, 64, 2))
+    assert plan(I8, M, 320, K, 128, 256, 1)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(BF, M, N, 128, 128, 64, 3)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(BF, M, N, 192, 128, 64, 3)[0] == 0                # bf16: K % 64
+    assert plan(BF, M, N, 1024, 256, 64, 5)[0] == _lib.FACK_ERR_BAD_ARG
 
 
 def test_check_maps_contract_violations_to_valueerror():

@@ -85,14 +85,16 @@ def test_golden_every_tile_and_split(cuda_device, name, packed):
         pytest.skip("the packed layout needs N % 128")
     b = fb.shuffle_weight(g["b"]) if packed else g["b"]
     chunks = g["k"] * (2 if g["fam"] == "bf16" else 1) // 128
-    for tile in (64, 128, 256):
-        if g["n"] % tile:
-            continue
-        for split in range(1, min(8, chunks) + 1):
-            out = poisoned(g["m"], g["n"], cuda_device)
-            run_family(g, out, b, splitK=split, kernelName=f"fack_tn_sm100_{g['fam']}_t128x{tile}_s{split}",
-                       bpreshuffle=packed)
-            check(out, g["reference"], g["fam"] == "i8", f"{name} tile={tile} split={split} packed={packed}")
+    for tile_m in (128, 256):                      # 256 = a CTA pair sharing each MMA
+        for tile in (64, 128, 256):
+            if g["n"] % tile:
+                continue
+            for split in range(1, min(8 if tile_m == 128 else 4, chunks) + 1):
+                out = poisoned(g["m"], g["n"], cuda_device)
+                run_family(g, out, b, splitK=split,
+                           kernelName=f"fack_tn_sm100_{g['fam']}_t{tile_m}x{tile}_s{split}", bpreshuffle=packed)
+                check(out, g["reference"], g["fam"] == "i8",
+                      f"{name} tile={tile_m}x{tile} split={split} packed={packed}")
 
 
 @pytest.mark.parametrize("m", [1, 96, 256, 300])
@@ -126,6 +128,29 @@ def test_bf16_shapes_vs_oracle(cuda_device, m):
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))   # same plan, same bits
 
 
+@pytest.mark.parametrize("kind", ["bf16", "i8"])
+def test_pairs_on_larger_shapes(cuda_device, kind):
+    """CTA-pair plans at 640 x 1536 x 2048 (row tiles off the 256 pair size) against the oracle."""
+    d = cuda_device
+    gen = torch.Generator().manual_seed(9)
+    M, N, K = 640 + 33, 1536, 2048
+    if kind == "bf16":
+        a = (torch.randn((M, K), generator=gen) * 0.25).bfloat16()
+        b = (torch.randn((N, K), generator=gen) * 0.25).bfloat16()
+        ref = sib.reference_bf16_tn(a, b)
+    else:
+        a = torch.randint(-128, 128, (M, K), generator=gen, dtype=torch.int8)
+        b = torch.randint(-128, 128, (N, K), generator=gen, dtype=torch.int8)
+        sa, sb = 0.001 + 0.01 * torch.rand(M, generator=gen), 0.001 + 0.01 * torch.rand(N, generator=gen)
+        ref = sib.reference_i8_per_token(a, b, sa, sb)
+    for packed in (False, True):
+        bb = fb.shuffle_weight(b.to(d)) if packed else b.to(d)
+        for tile, split in ((256, 1), (128, 2), (64, 4), (256, 3)):
+            kw = {} if kind == "bf16" else {"a_scale": sa.to(d), "b_scale": sb.to(d)}
+            y = fb.gemm_tn(a.to(d), bb, tile_m=256, tile_n=tile, split_k=split, **kw)
+            check(y, ref, kind == "i8", f"{kind} pair 256x{tile} split={split} packed={packed}")
+
+
 def test_split_k_bitwise_reproducible_and_strided_out(cuda_device):
     d = cuda_device
     gen = torch.Generator().manual_seed(5)
@@ -143,7 +168,7 @@ def test_split_k_bitwise_reproducible_and_strided_out(cuda_device):
 
 def test_public_config_and_contract_errors(cuda_device):
     cfg = siblings.get_config(siblings.KINDS[torch.int8], 256, 3072, 7168)
-    assert cfg["kernelName"].startswith("fack_tn_sm100_i8_t128x") and cfg["splitK"] >= 1
+    assert cfg["kernelName"].startswith("fack_tn_sm100_i8_t") and cfg["splitK"] >= 1
     d = cuda_device
     a = torch.zeros((4, 256), dtype=torch.int8, device=d)
     b = torch.zeros((256, 256), dtype=torch.int8, device=d)
