@@ -16,8 +16,10 @@ set; steps rotate over enough distinct input sets that the rotation exceeds
 ``--gpus N`` under torchrun: the decode / plumbing / sweep workloads do not
 shard, so N ranks run N independent replicas (weak scaling, no collective).
 ``--workload prefill|wide_constant|wide_uniform`` shards the output columns
-over the ranks and all-gathers the bf16 output over NCCL every step (strong
-scaling).
+over the ranks (strong scaling); every step each rank's GEMM epilogue stores
+its bf16 column block into every rank's Y over NVLink peer mappings, between
+two one-element NCCL all-reduces (``--gather fused``, the default), or the
+blocks are all-gathered over NCCL and interleaved (``--gather nccl``).
 
 ``--impl reference`` times the reference's own algorithm for this path -- the
 fp32 dequantise-then-matmul of client/aiter/hsa/gfx942/driver.py:18-20 -- on
@@ -251,7 +253,7 @@ def run_ours(args):
     sharder = None
     if sharded:
         from fack_b200.dist import ShardedBlockscaleGemm
-        sharder = ShardedBlockscaleGemm()
+        sharder = ShardedBlockscaleGemm(mode=args.gather)
         full_out = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(n_sets)]
 
     def gemm_call(s):
@@ -381,7 +383,9 @@ def run_ours(args):
         cpu = {"value": round(tfl, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample}
 
     clocks = sampler.summary()
-    per_step_launches = 2 if sharded else 1  # GEMM (+ column interleave when sharded)
+    # GEMM (+ the column interleave of the NCCL-gather path); the fused path's
+    # two one-element all-reduces per step are NCCL's kernels, not counted
+    per_step_launches = 2 if sharded and args.gather == "nccl" else 1
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 6), "higher_is_better": True,
@@ -393,7 +397,10 @@ def run_ours(args):
                    "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB = {n_sets * set_bytes / 1e6:.0f} MB"
                          f" (> 126 MB L2)",
                    "timing": f"{timing}, CUDA events on the launch stream, max over ranks",
-                   "parallelism": (f"N-shard g={world} + NCCL all-gather" if sharded else
+                   "parallelism": ((f"N-shard g={world}: GEMM epilogue stores every tile to all ranks' Y over "
+                                    "NVLink peer mappings (CUDA IPC), 1-element NCCL all-reduce barriers"
+                                    if args.gather == "fused" else f"N-shard g={world} + NCCL all-gather")
+                                   if sharded else
                                    ("single GPU" if world == 1 else f"{world} independent replicas"))},
         "us_per_call": round(us_call, 3), "hbm_gbs": round(data.algorithmic_bytes(wl.M, n_local, wl.K) /
                                                            (k_us * 1e3), 1),
@@ -410,6 +417,9 @@ def run_ours(args):
     del graphs, plan, probe, run_chunk, run_rem, run_gemm
     if world > 1:
         torch.cuda.synchronize()
+        dist.barrier()
+        if sharder is not None:
+            sharder.close()  # release the peer mappings before the group goes
         dist.barrier()
         dist.destroy_process_group()
     if status:
@@ -505,6 +515,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="sharded workloads: peer stores from the GEMM epilogue, or NCCL all-gather + interleave")
     ap.add_argument("--rotate", type=int, default=0, help="input sets to rotate (0 = enough to exceed L2)")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--no-e2e", action="store_true")

@@ -66,6 +66,12 @@ SIGNATURES = {
     "fack_gemm_tn_plan": (_c_int, [_c_int] * 7 + [ctypes.POINTER(_c_int)] * 3),
     "fack_gemm_tn": (_c_int, [_c_int, _c_p, _c_i64, _c_p, _c_int, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64,
                               _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p]),
+    "fack_gemm_bs_bcast": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
+                                    ctypes.POINTER(_c_p), _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                    _c_p, _c_sz, _c_p]),
+    "fack_ipc_get_handle": (_c_int, [_c_p, _c_p, _c_sz, ctypes.POINTER(_c_sz)]),
+    "fack_ipc_open_handle": (_c_int, [_c_p, ctypes.POINTER(_c_p)]),
+    "fack_ipc_close_handle": (_c_int, [_c_p]),
     "fack_gemm_bs_tuned_set": (_c_int, [_c_int] * 7),
     "fack_gemm_bs_tuned_lookup": (_c_int, [_c_int] * 4 + [ctypes.POINTER(_c_int)] * 3),
     "fack_gemm_bs_tuned_count": (_c_int, []),

@@ -112,12 +112,18 @@ struct Cfg {
   static_assert(kTileM * kPitch32 * 4 <= kOffRaw, "fp32 output staging must fit in the stage ring");
 };
 
+constexpr int kMaxPeers = 7;  // peer outputs of fack_gemm_bs_bcast (8 GPUs per node)
+
 struct Params {
   const float* x_scale;
   int64_t xs_sm, xs_sk;
   const float* w_scale;        // [N/128][K/128]
   __nv_bfloat16* out;
   int64_t ldo;
+  // the same output block in other GPUs' memory (peer mappings, same ldo):
+  // every bf16 result is stored to out and to each peer_out[0..n_peer)
+  __nv_bfloat16* peer_out[kMaxPeers];
+  int n_peer;
   float* partials;             // [tiles][S][128][BN] fp32 for S > 1; NULL = reduce through DSMEM
   int M, N, K, KB;
   int split;
@@ -125,13 +131,23 @@ struct Params {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float4& v) {
+__device__ __forceinline__ uint2 pack_bf16x4(const float4& v) {
   __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
   __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
   uint2 pk;
   pk.x = *reinterpret_cast<uint32_t*>(&lo);
   pk.y = *reinterpret_cast<uint32_t*>(&hi);
-  *reinterpret_cast<uint2*>(dst) = pk;
+  return pk;
+}
+
+// Element offset `off` of the output: this GPU's copy, then each peer's.
+__device__ __forceinline__ void store_out8(const Params& p, int64_t off, const uint2& v) {
+  *reinterpret_cast<uint2*>(p.out + off) = v;
+  for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint2*>(p.peer_out[d] + off) = v;
+}
+__device__ __forceinline__ void store_out16(const Params& p, int64_t off, const uint4& v) {
+  *reinterpret_cast<uint4*>(p.out + off) = v;
+  for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint4*>(p.peer_out[d] + off) = v;
 }
 
 // Split-K reduction over distributed shared memory: rows [r0, r1) of the
@@ -141,7 +157,7 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float4& v
 // its registers are allocated apart from the rescale loop.
 template <int BN, int PITCH>
 __device__ __noinline__ void reduce_dsmem(uint32_t stg, int S, int rank0, int rank_step, int r0, int r1,
-                                          __nv_bfloat16* out, int64_t ldo) {
+                                          const Params& p, int64_t off0) {
   constexpr int kRowF4 = BN / 4;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
   for (int it = threadIdx.x; it < items; it += kThreads) {
@@ -156,7 +172,7 @@ __device__ __noinline__ void reduce_dsmem(uint32_t stg, int S, int rank0, int ra
       sum.z += v.z;
       sum.w += v.w;
     }
-    store_bf16x4(out + r * ldo + c4 * 4, sum);
+    store_out8(p, off0 + r * p.ldo + c4 * 4, pack_bf16x4(sum));
   }
 }
 
@@ -182,7 +198,7 @@ __device__ __noinline__ void copy_partial(const float* stg, int rows, int keep0,
 // the others from the workspace (L2).
 template <int BN, int PITCH>
 __device__ __noinline__ void reduce_global(const float* part0, const float* stg, int self, int S, int r0, int r1,
-                                           __nv_bfloat16* out, int64_t ldo) {
+                                           const Params& p, int64_t off0) {
   constexpr int kRowF4 = BN / 4;
   const int items = (r1 > r0 ? r1 - r0 : 0) * kRowF4;
   for (int it = threadIdx.x; it < items; it += kThreads) {
@@ -201,7 +217,7 @@ __device__ __noinline__ void reduce_global(const float* part0, const float* stg,
         sum.w += v.w;
       }
     }
-    store_bf16x4(out + r * ldo + c, sum);
+    store_out8(p, off0 + r * p.ldo + c, pack_bf16x4(sum));
   }
 }
 
@@ -605,8 +621,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     for (int c = threadIdx.x; c < rows * kRowChunks; c += kThreads) {
       const int r = c / kRowChunks, cc = c % kRowChunks;
       const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
-      *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8) = v;
+      store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
     }
+    if (p.n_peer) __threadfence_system();  // peer stores are visible before this grid completes
     return;
   }
 
@@ -625,8 +642,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // its shared memory) alive until all peers have finished reading.
     cluster_sync_all();
     if (ok)
-      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1,
-                                    p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1, p,
+                                    static_cast<int64_t>(m0) * p.ldo + n0);
+    if (p.n_peer) __threadfence_system();
     cluster_sync_all();
     return;
   }
@@ -642,8 +660,9 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   cluster_sync_all();
   if (!ok) return;
-  reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1,
-                                 p.out + static_cast<int64_t>(m0) * p.ldo + n0, p.ldo);
+  reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1, p,
+                                 static_cast<int64_t>(m0) * p.ldo + n0);
+  if (p.n_peer) __threadfence_system();
 }
 
 // ------------------------------------------------------------------ prepack --
@@ -1106,11 +1125,18 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, in
   return FACK_OK;
 }
 
-int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
-                    int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
-                    int N, int K, int tile_m, int tile_n, int split_k, void* workspace, size_t workspace_bytes,
-                    void* stream) {
+}  // extern "C"
+
+// fack_gemm_bs_ex with the result also stored to n_peers peer copies of the
+// output block (same ldo); n_peers = 0 is fack_gemm_bs_ex.
+static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                        int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                        void* const* peer_outs, int n_peers, int M, int N, int K, int tile_m, int tile_n,
+                        int split_k, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_outs)) return FACK_ERR_BAD_ARG;
+  for (int i = 0; i < n_peers; ++i)
+    if (!peer_outs[i] || !aligned(peer_outs[i], 16)) return FACK_ERR_BAD_ALIGN;
   if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
   if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
   if (!xq || !wq || !out || !x_scale || !w_scale) return FACK_ERR_BAD_ALIGN;
@@ -1149,6 +1175,9 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
   p.w_scale = w_scale;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
+  p.n_peer = n_peers;
+  for (int i = 0; i < kMaxPeers; ++i)
+    p.peer_out[i] = i < n_peers ? static_cast<__nv_bfloat16*>(peer_outs[i]) : nullptr;
   p.partials = static_cast<float*>(workspace);
   p.M = M;
   p.N = N;
@@ -1160,6 +1189,66 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return launch(d, tm, bn, tw, tx, p, M, s);
+}
+
+extern "C" {
+
+int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                    int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo, int M,
+                    int N, int K, int tile_m, int tile_n, int split_k, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  return gemm_bs_impl(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, nullptr, 0, M,
+                      N, K, tile_m, tile_n, split_k, workspace, workspace_bytes, stream);
+}
+
+int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                       int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                       void* const* peer_outs, int n_peers, int M, int N, int K, int tile_m, int tile_n, int split_k,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_bs_impl(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, peer_outs,
+                      n_peers, M, N, K, tile_m, tile_n, split_k, workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------ CUDA IPC --
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int fack_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes, size_t* offset) {
+  if (!ptr || !handle || !offset || handle_bytes < sizeof(cudaIpcMemHandle_t)) return FACK_ERR_BAD_ARG;
+  static AddressRangeFn range = nullptr;
+  if (!range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return fail(FACK_ERR_CUDA, "cuMemGetAddressRange entry point");
+    range = reinterpret_cast<AddressRangeFn>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(FACK_ERR_BAD_ARG, "pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(FACK_ERR_CUDA, "cudaIpcGetMemHandle", e);
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return FACK_OK;
+}
+
+int fack_ipc_open_handle(const void* handle, void** base) {
+  if (!handle || !base) return FACK_ERR_BAD_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(FACK_ERR_CUDA, "cudaIpcOpenMemHandle", e);
+  return FACK_OK;
+}
+
+int fack_ipc_close_handle(void* base) {
+  if (!base) return FACK_ERR_BAD_ARG;
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return fail(FACK_ERR_CUDA, "cudaIpcCloseMemHandle", e);
+  return FACK_OK;
 }
 
 int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,

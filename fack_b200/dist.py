@@ -3,10 +3,18 @@
 The reference runs one GPU per process and has no collective
 (client/aiter/docs/validation.md:42-46).  For the wide and prefill layers this
 library shards the output columns: rank r owns WQ rows [r*N/g, (r+1)*N/g) and
-the matching w_scale rows, the activations are replicated, each rank computes
-its [M, N/g] block with the single-GPU kernel straight into its slot of a
-[g, M, N/g] gather buffer, an in-place all-gather (NCCL over NVLink) fills the
-other slots, and a column-interleave kernel assembles row-major Y[M, N].
+the matching w_scale rows, the activations are replicated, and each rank
+computes its [M, N/g] block with the single-GPU kernel.  Two ways to assemble
+the replicated row-major Y[M, N]:
+
+* ``mode="fused"`` (GPUs): the GEMM's own epilogue stores each bf16 tile into
+  column block r of every rank's Y through NVLink peer mappings (CUDA IPC;
+  ``fack_gemm_bs_bcast``), so the exchange overlaps the math tile by tile and
+  no separate gather or interleave runs; a one-element all-reduce before and
+  after the launch, on the same stream, orders it against the other ranks.
+* ``mode="nccl"``: the block goes to this rank's slot of a [g, M, N/g] gather
+  buffer, an in-place NCCL all-gather fills the other slots, and a
+  column-interleave kernel assembles Y (also the gloo path of the CPU tests).
 
 Only the bf16 output crosses NVLink; N/g stays a multiple of 128, so every
 shard is made of whole 128x128 weight-scale blocks.
@@ -47,23 +55,93 @@ def _default_interleave(gathered, out):
     return gather_interleave(gathered, out)
 
 
+def _default_local_gemm_peers(xq, wq, x_scale, w_scale, out, peer_addrs):
+    from .ops import gemm_blockscale
+    return gemm_blockscale(xq, wq, x_scale, w_scale, out=out, peer_outs=peer_addrs)
+
+
+class CudaIpc:
+    """Peer mappings through the library's CUDA IPC entry points."""
+
+    HANDLE_BYTES = 64
+
+    def handle(self, t: torch.Tensor) -> tuple:
+        from . import _lib
+        import ctypes
+        lib = _lib.load()
+        buf = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        off = ctypes.c_size_t()
+        _lib.check(lib.fack_ipc_get_handle(t.data_ptr(), buf, self.HANDLE_BYTES, ctypes.byref(off)),
+                   "fack_ipc_get_handle")
+        return buf.raw, off.value
+
+    def open(self, handle: bytes) -> int:
+        from . import _lib
+        import ctypes
+        lib = _lib.load()
+        base = ctypes.c_void_p()
+        _lib.check(lib.fack_ipc_open_handle(ctypes.create_string_buffer(handle, len(handle)), ctypes.byref(base)),
+                   "fack_ipc_open_handle")
+        return int(base.value)
+
+    def close(self, base: int) -> None:
+        from . import _lib
+        _lib.load().fack_ipc_close_handle(base)
+
+
+def exchange_peer_addresses(t: torch.Tensor, ipc, group=None) -> list:
+    """Collective: every rank publishes (IPC handle, offset) of its tensor ``t``
+    and maps every other rank's.  Returns, for each rank j != this rank in rank
+    order, (mapped base, address of j's ``t``)."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    h, off = ipc.handle(t)
+    hb = ipc.HANDLE_BYTES
+    if len(h) != hb:
+        raise ValueError("IPC handle size mismatch")
+    rec = torch.tensor(list(h) + list(int(off).to_bytes(8, "little")), dtype=torch.uint8)
+    if dist.get_backend(group) == "nccl":
+        rec = rec.to(t.device)
+    recs = [torch.empty_like(rec) for _ in range(world)]
+    dist.all_gather(recs, rec, group=group)
+    peers = []
+    for j, r in enumerate(recs):
+        if j == rank:
+            continue
+        raw = bytes(r.cpu().tolist())
+        base = ipc.open(raw[:hb])
+        peers.append((base, base + int.from_bytes(raw[hb:hb + 8], "little")))
+    return peers
+
+
 class ShardedBlockscaleGemm:
     """Y[M, N] = blockscale(XQ, WQ) with WQ column-sharded over a process group.
 
-    ``local_gemm(xq, wq_shard, x_scale, ws_shard, out)`` and
+    ``mode="nccl"``: ``local_gemm(xq, wq_shard, x_scale, ws_shard, out)`` and
     ``interleave(gathered, out)`` default to this library's CUDA kernels; the
     CPU tests substitute checkers to exercise the sharding and gather logic
-    on gloo ranks.
+    on gloo ranks.  ``mode="fused"``: ``out`` (row-major [M, N], required)
+    is registered with every rank on first use (a collective: all ranks pass
+    their buffers in the same order, outside CUDA-graph capture), then each
+    call is barrier -> GEMM storing to every rank's ``out`` -> barrier.
     """
 
     def __init__(self, group=None, local_gemm: Optional[Callable] = None,
-                 interleave: Optional[Callable] = None):
+                 interleave: Optional[Callable] = None, mode: str = "nccl", ipc=None,
+                 local_gemm_peers: Optional[Callable] = None):
+        if mode not in ("nccl", "fused"):
+            raise ValueError("mode must be 'nccl' or 'fused'")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.mode = mode
         self.local_gemm = local_gemm or _default_local_gemm
+        self.local_gemm_peers = local_gemm_peers or _default_local_gemm_peers
         self.interleave = interleave or _default_interleave
+        self.ipc = ipc
         self._gather = None
+        self._peers: dict = {}     # (data_ptr, numel) of a registered out -> peer addresses of the same buffer
+        self._mapped: list = []    # mapped peer bases, released by close()
+        self._flag = None
 
     def gather_buffer(self, M: int, ns: int, device) -> torch.Tensor:
         g = self._gather
@@ -74,11 +152,46 @@ class ShardedBlockscaleGemm:
             self._gather = g
         return g
 
+    def register(self, out: torch.Tensor) -> list:
+        """Peer addresses of ``out`` on the other ranks (collective on first use)."""
+        key = (out.data_ptr(), out.numel())
+        if key not in self._peers:
+            if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("register output buffers before CUDA-graph capture")
+            if self.ipc is None:
+                self.ipc = CudaIpc()
+            pairs = exchange_peer_addresses(out, self.ipc, self.group)
+            self._mapped += [base for base, _ in pairs]
+            self._peers[key] = [addr for _, addr in pairs]
+        return self._peers[key]
+
+    def _barrier(self, device) -> None:
+        if self._flag is None or self._flag.device != torch.device(device):
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        """Release the peer mappings (before the process group is destroyed)."""
+        for base in self._mapped:
+            self.ipc.close(base)
+        self._mapped, self._peers = [], {}
+
     def __call__(self, xq, wq_shard, x_scale, ws_shard, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         M = xq.shape[0]
         ns = wq_shard.shape[0]
         if ns % BLOCK:
             raise ValueError("weight shard must hold whole 128-row blocks")
+        if self.mode == "fused":
+            if out is None or tuple(out.shape) != (M, self.world * ns) or not out.is_contiguous():
+                raise ValueError(f"fused mode needs a contiguous out of shape [{M}, {self.world * ns}]")
+            peers = self.register(out)
+            col = self.rank * ns
+            nbytes = out.element_size() * col                 # byte offset of this rank's column block
+            self._barrier(out.device)                         # no rank still reads the Y about to be written
+            self.local_gemm_peers(xq, wq_shard, x_scale, ws_shard, out[:, col:col + ns],
+                                  [a + nbytes for a in peers])
+            self._barrier(out.device)                         # every rank's blocks have landed everywhere
+            return out
         gathered = self.gather_buffer(M, ns, xq.device)
         mine = gathered[self.rank]
         self.local_gemm(xq, wq_shard, x_scale, ws_shard, mine)

@@ -146,10 +146,12 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
 
 
 def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m=0, tile_n=0,
-            reduce="dsmem"):
+            reduce="dsmem", peer_outs=()):
     """reduce = "dsmem": split-K slices combine through the cluster's shared
     memory (no workspace, nothing allocated); "global": through a cached
-    workspace in global memory."""
+    workspace in global memory.  ``peer_outs``: device addresses (this
+    process's mappings of other GPUs' memory) of more copies of ``out``'s
+    block, same row stride; every result is stored to each of them too."""
     M, K = xq.shape
     N = wq.shape[0]
     dev = xq.device
@@ -157,22 +159,31 @@ def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m
     with torch.cuda.device(dev):
         tm, tn, sk, need = plan(M, N, K, tile_m, tile_n, split_k)
         ws = _workspace(dev, need) if reduce == "global" else None
-        st = lib.fack_gemm_bs_ex(
-            xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
-            x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0),
-            M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
-    _lib.check(st, "fack_gemm_bs_ex")
+        args = (xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
+                x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0))
+        tail = (M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
+        if peer_outs:
+            peers = (ctypes.c_void_p * len(peer_outs))(*[int(a) for a in peer_outs])
+            st = lib.fack_gemm_bs_bcast(*args, peers, len(peer_outs), *tail)
+        else:
+            st = lib.fack_gemm_bs_ex(*args, *tail)
+    _lib.check(st, "fack_gemm_bs_bcast" if peer_outs else "fack_gemm_bs_ex")
     return out
 
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                     out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0, tile_m: int = 0,
-                    reduce: str = "dsmem") -> torch.Tensor:
+                    reduce: str = "dsmem", peer_outs=()) -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
     :func:`shuffle_weight` (detected by its ``is_shuffled`` mark).
+    ``peer_outs`` (up to 7 device addresses of peer mappings, each the same
+    block as ``out`` in another GPU's output, same row stride) makes the
+    kernel store every result there too (``fack_gemm_bs_bcast``).
     """
+    if len(peer_outs) > 7:
+        raise ValueError("at most 7 peer outputs")
     if xq.dim() != 2 or wq.dim() != 2:
         raise ValueError("XQ and WQ must be 2-D")
     M, K = xq.shape
@@ -190,7 +201,7 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
     if reduce not in ("dsmem", "global"):
         raise ValueError("reduce must be 'dsmem' or 'global'")
     return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_m,
-                   tile_n, reduce)
+                   tile_n, reduce, tuple(peer_outs))
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):

@@ -106,6 +106,35 @@ int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
                         int* tile_n, int* split_k);
 
 /*
+ * fack_gemm_bs_ex that also stores every bf16 result to n_peers (0..7) more
+ * copies of the output block, peer_outs[i] + (row * ldo + column), with the
+ * same ldo: the fused compute + all-gather of the column-sharded multi-GPU
+ * path, where rank r writes its [M, N/g] block straight into every rank's
+ * row-major Y[M, N] (out and each peer_outs[i] point at column r * N/g of a
+ * rank's Y).  peer_outs are this process's mappings of other GPUs' memory
+ * (fack_ipc_open_handle), 16-byte aligned; plain stores over NVLink, no
+ * multicast.  The caller orders the launch between two barriers across the
+ * ranks (e.g. a one-element all-reduce on the same stream): before it, so no
+ * rank overwrites a Y another rank still reads; after it, so every rank's Y is
+ * complete.  The kernel ends its peer stores with a system-scope fence.
+ */
+int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                       int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                       void* const* peer_outs, int n_peers, int M, int N, int K, int tile_m, int tile_n, int split_k,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * CUDA IPC for the peer outputs.  fack_ipc_get_handle: the IPC handle (64
+ * bytes into `handle`, handle_bytes >= 64) of the allocation holding `ptr` and
+ * ptr's byte offset inside it (allocators hand out sub-ranges).  Another
+ * process on the node opens the handle with fack_ipc_open_handle, adds the
+ * offset, and releases it with fack_ipc_close_handle.
+ */
+int fack_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes, size_t* offset);
+int fack_ipc_open_handle(const void* handle, void** base);
+int fack_ipc_close_handle(void* base);
+
+/*
  * Exact-shape plan table, the B200 counterpart of aiter's tuned GEMM CSV
  * (rows keyed by cu_num, M, N, K with kernelName and splitK;
  * client/aiter/dispatch.py:23-35, exact match only, dispatch.py:3-6).  Rows

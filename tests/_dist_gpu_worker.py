@@ -36,6 +36,17 @@ def main():
             ok &= torch.equal(y[:, n0:n1].view(torch.int16), local_r.view(torch.int16))
         ok &= bool(torch.allclose(y.float(), full.float(), rtol=1e-2, atol=1e-2))
         ok &= fb.device_status() == 0
+        # fused: the GEMM's epilogue stores into every rank's Y over NVLink
+        fused = ShardedBlockscaleGemm(mode="fused")
+        y_f = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+        for _ in range(2):                                         # registered once, reused
+            fused(xq, fb.shuffle_weight(wq_r), xs, ws_r, out=y_f)
+            torch.cuda.synchronize()
+            ok &= torch.equal(y_f.view(torch.int16), y.view(torch.int16))
+            y_f.fill_(float("nan"))
+            dist.barrier()
+        fused.close()
+        ok &= fb.device_status() == 0
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()

@@ -93,3 +93,83 @@ def test_shard_bounds_and_weight_slices():
     w1, s1 = shard_weight(wq, ws, 1, 2)
     assert w1.shape == (256, 256) and torch.equal(s1, ws[2:4])
     assert torch.equal(w1.view(torch.uint8), wq[256:512].view(torch.uint8))
+
+
+# ---------------------------------------------------------------- fused mode --
+# The fused path stores each rank's block into every rank's Y through peer
+# mappings.  On CPU ranks the "GPU memory" of rank j is a shared-memory tensor
+# ys[j]; the fake IPC layer hands out addresses (j + 1) << 40 + byte offset, and
+# the fake GEMM resolves them, so the test checks the handle exchange, the
+# offset arithmetic and the barrier order of the real ShardedBlockscaleGemm.
+
+class _FakeIpc:
+    HANDLE_BYTES = 64
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened, self.closed = [], []
+
+    def handle(self, t):
+        return bytes([self.rank]) + bytes(63), 0   # this rank's Y starts at its mapping's base
+
+    def open(self, handle):
+        j = handle[0]
+        self.opened.append(j)
+        return (j + 1) << 40
+
+    def close(self, base):
+        self.closed.append(base)
+
+
+def _fused_worker(rank, world, port, M, N, K, ys):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from fack_b200 import data
+        from fack_b200.dist import ShardedBlockscaleGemm, shard_weight
+        from oracle.blockscale import reference_gemm
+        xq, xs, wq, ws = data.make_inputs(data.Workload("dist", M, N, K), seed=4)
+        wq_r, ws_r = shard_weight(wq, ws, rank, world)
+
+        def local(xq_, wq_, xs_, ws_, out_view, peer_addrs):
+            block = reference_gemm(xq_, wq_, xs_, ws_)
+            out_view.copy_(block)
+            assert len(peer_addrs) == world - 1
+            for a in peer_addrs:
+                j = (a >> 40) - 1
+                assert j != rank and 0 <= j < world
+                col = (a & ((1 << 40) - 1)) // 2          # byte offset inside Y_j, row 0
+                ys[j][:, col:col + block.shape[1]].copy_(block)
+
+        ipc = _FakeIpc(rank)
+        gemm = ShardedBlockscaleGemm(mode="fused", ipc=ipc, local_gemm_peers=local)
+        y = gemm(xq, wq_r, xs, ws_r, out=ys[rank])
+        assert y is ys[rank]
+        gemm(xq, wq_r, xs, ws_r, out=ys[rank])            # registered once: no second exchange
+        assert sorted(ipc.opened) == [j for j in range(world) if j != rank]
+        gemm.close()
+        assert len(ipc.closed) == world - 1
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_mode_two_gloo_ranks():
+    world, M, N, K = 2, 33, 768, 384
+    ys = [torch.full((M, N), float("nan"), dtype=torch.bfloat16).share_memory_() for _ in range(world)]
+    mp.start_processes(_fused_worker, args=(world, _free_port(), M, N, K, ys), nprocs=world,
+                       start_method="spawn", join=True)
+    from fack_b200 import data
+    from fack_b200.dist import shard_weight
+    from oracle.blockscale import reference_gemm
+    xq, xs, wq, ws = data.make_inputs(data.Workload("dist", M, N, K), seed=4)
+    exact = torch.cat([reference_gemm(xq, *shard_weight(wq, ws, r, world)[:1], xs, shard_weight(wq, ws, r, world)[1])
+                       for r in range(world)], dim=1)
+    for r in range(world):
+        assert torch.equal(ys[r].view(torch.int16), exact.view(torch.int16)), f"rank {r}'s Y"
+
+
+def test_fused_mode_contract():
+    from fack_b200.dist import ShardedBlockscaleGemm
+    with pytest.raises(ValueError):
+        ShardedBlockscaleGemm.__init__(object.__new__(ShardedBlockscaleGemm), mode="ring")
