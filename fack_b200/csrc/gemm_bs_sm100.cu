@@ -140,14 +140,15 @@ __device__ __forceinline__ uint2 pack_bf16x4(const float4& v) {
   return pk;
 }
 
-// Element offset `off` of the output: this GPU's copy, then each peer's.
+// Element offset `off` of the output: each peer's copy first (the NVLink
+// stores have the longer way to go), then this GPU's.
 __device__ __forceinline__ void store_out8(const Params& p, int64_t off, const uint2& v) {
-  *reinterpret_cast<uint2*>(p.out + off) = v;
   for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint2*>(p.peer_out[d] + off) = v;
+  *reinterpret_cast<uint2*>(p.out + off) = v;
 }
 __device__ __forceinline__ void store_out16(const Params& p, int64_t off, const uint4& v) {
-  *reinterpret_cast<uint4*>(p.out + off) = v;
   for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint4*>(p.peer_out[d] + off) = v;
+  *reinterpret_cast<uint4*>(p.out + off) = v;
 }
 
 // Split-K reduction over distributed shared memory: rows [r0, r1) of the
