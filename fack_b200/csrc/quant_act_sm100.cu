@@ -14,9 +14,9 @@
 // <= 16 KB) with 1-D bulk copies into a 4-stage ring, so the bytes in flight sit in
 // shared memory rather than registers; sixteen warps each take two groups at
 // a time from the landed chunk (4 elements per lane), reduce its amax with
-// shuffles, divide with IEEE division, convert with the hardware
-// round-to-nearest-even e4m3 conversion and store 4 codes per lane (128 B per
-// warp).  Every mbarrier wait is bounded; on expiry the CTA records a flag in
+// one warp-wide integer max (redux.sync) on the magnitudes' bit patterns,
+// divide with IEEE division, convert with the hardware round-to-nearest-even
+// e4m3 conversion and store 4 codes per lane (128 B per warp).  Every mbarrier wait is bounded; on expiry the CTA records a flag in
 // the library's device status word, drains its copies and exits.
 
 #include <cuda.h>
@@ -143,11 +143,10 @@ __global__ void __launch_bounds__(kQThreads, 2) quant_act_kernel(const T* __rest
 #pragma unroll
         for (int u = 0; u < 2; ++u)
           a[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], o));
-          a[1] = fmaxf(a[1], __shfl_xor_sync(0xffffffffu, a[1], o));
-        }
+        // warp maximum in one instruction each: for non-negative floats the bit
+        // patterns order as unsigned integers
+        a[0] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a[0])));
+        a[1] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a[1])));
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           if (u == 1 && !two) break;
