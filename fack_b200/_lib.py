@@ -69,7 +69,6 @@ SIGNATURES = {
     "fack_gemm_bs_bcast": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                                     ctypes.POINTER(_c_p), _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                     _c_p, _c_sz, _c_p]),
-    "fack_gemm_bs_launches": (_c_int, [_c_int] * 6 + [ctypes.POINTER(_c_int)]),
     "fack_ipc_get_handle": (_c_int, [_c_p, _c_p, _c_sz, ctypes.POINTER(_c_sz)]),
     "fack_ipc_open_handle": (_c_int, [_c_p, ctypes.POINTER(_c_p)]),
     "fack_ipc_close_handle": (_c_int, [_c_p]),

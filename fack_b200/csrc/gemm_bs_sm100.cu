@@ -128,8 +128,6 @@ struct Params {
   int M, N, K, KB;
   int split;
   int w_packed;
-  int tiles_n, tiles_m;        // single-CTA plans: output tiles along N and M
-  int lin_base;                // single-CTA plans: first tile (grouped order) of this launch
   uint64_t timeout_ns;
 };
 
@@ -268,12 +266,10 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   int mt, nt;
   {
     const int unit = PAIR ? 2 : 1;                               // CTAs per token-tile slot
-    // single CTAs run a 1-D grid over tiles [lin_base, lin_base + gridDim.x)
-    // of the tiles_n x tiles_m tile grid (a launch may cover part of it)
-    const int m_slots = PAIR ? static_cast<int>(gridDim.x) / 2 : p.tiles_m;
-    const int n_tiles = PAIR ? static_cast<int>(gridDim.y) : p.tiles_n;
+    const int m_slots = PAIR ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.y);
+    const int n_tiles = PAIR ? static_cast<int>(gridDim.y) : static_cast<int>(gridDim.x);
     const int lin = PAIR ? static_cast<int>(blockIdx.x) / 2 + static_cast<int>(blockIdx.y) * m_slots
-                         : p.lin_base + static_cast<int>(blockIdx.x);
+                         : static_cast<int>(blockIdx.x) + static_cast<int>(blockIdx.y) * n_tiles;
     const int per_group = kGroupM * n_tiles;
     const int g = lin / per_group;
     const int first = g * kGroupM;
@@ -972,14 +968,16 @@ static int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS ? FACK_OK : FACK_ERR_BAD_ALIGN;
 }
 
-static int launch_grid(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
-                       dim3 grid, cudaStream_t stream) {
+static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
+                  int M, cudaStream_t stream) {
   const int st = ensure_configured(d, tm, bn);
   if (st != FACK_OK) return st;
   const KernelEntry& k = kernel_for(tm, bn);
+  int gx, gy, gz;
+  plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = grid;
+  cfg.gridDim = dim3(gx, gy, gz);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = stream;
@@ -1002,54 +1000,6 @@ static int launch_grid(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, con
   const cudaError_t e = cudaLaunchKernelExC(&cfg, k.fn, args);
   if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaLaunchKernelExC", e);
   return FACK_OK;
-}
-
-// Tail split: an unsplit single-CTA plan whose last wave would hold only a few
-// tiles (at most a quarter of the co-resident CTAs) runs those tiles first in
-// a launch of their own, split over K in clusters (reduced through
-// distributed shared memory), then the other tiles as whole waves.  The tail
-// then takes ~1/S of a tile's time instead of a whole wave.  Returns the
-// tail's split (0: no tail launch) and its tile count.
-static int tail_split(DeviceInfo* d, int M, int N, int K, int tm, int bn, int sp, int* tail_tiles) {
-  *tail_tiles = 0;
-  if (tm != kTileM || sp != 1) return 0;
-  const int KB = K / kBlk;
-  const int tiles = (N / bn) * ((M + kTileM - 1) / kTileM);
-  const int slots = co_resident(d, tm, bn, 1);
-  if (slots <= 0 || tiles <= slots || KB < 16) return 0;
-  const int tail = tiles % slots;
-  if (tail == 0 || 4 * tail > slots) return 0;
-  for (int s = kMaxSplit; s >= 2; --s) {
-    if (s * tail > slots || KB / s < 4) continue;
-    if (co_resident(d, tm, bn, s) < tail) continue;  // all tail clusters fit at once
-    *tail_tiles = tail;
-    return s;
-  }
-  return 0;
-}
-
-static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CUtensorMap& tx, Params p, int M,
-                  cudaStream_t stream) {
-  if (tm == 256) {
-    int gx, gy, gz;
-    plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
-    return launch_grid(d, tm, bn, tw, tx, p, dim3(gx, gy, gz), stream);
-  }
-  p.tiles_n = p.N / bn;
-  p.tiles_m = (M + kTileM - 1) / kTileM;
-  const int tiles = p.tiles_n * p.tiles_m;
-  int tail = 0;
-  const int ts = tail_split(d, M, p.N, p.K, tm, bn, p.split, &tail);
-  if (ts) {
-    Params pt = p;
-    pt.split = ts;
-    pt.partials = nullptr;  // combined through distributed shared memory
-    pt.lin_base = tiles - tail;
-    const int st = launch_grid(d, tm, bn, tw, tx, pt, dim3(tail, 1, ts), stream);
-    if (st != FACK_OK) return st;
-  }
-  p.lin_base = 0;
-  return launch_grid(d, tm, bn, tw, tx, p, dim3(tiles - tail, 1, p.split), stream);
 }
 
 static bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -1226,9 +1176,6 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   p.w_scale = w_scale;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
-  p.tiles_n = N / bn;
-  p.tiles_m = (M + kTileM - 1) / kTileM;
-  p.lin_base = 0;
   p.n_peer = n_peers;
   for (int i = 0; i < kMaxPeers; ++i)
     p.peer_out[i] = i < n_peers ? static_cast<__nv_bfloat16*>(peer_outs[i]) : nullptr;
@@ -1253,19 +1200,6 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed, 
                     void* stream) {
   return gemm_bs_impl(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, nullptr, 0, M,
                       N, K, tile_m, tile_n, split_k, workspace, workspace_bytes, stream);
-}
-
-int fack_gemm_bs_launches(int M, int N, int K, int tile_m, int tile_n, int split_k, int* launches) {
-  if (!launches) return FACK_ERR_BAD_ARG;
-  int tm = 0, bn = 0, sp = 0;
-  int st = fack_gemm_bs_plan(M, N, K, tile_m, tile_n, split_k, &tm, &bn, &sp, nullptr);
-  if (st != FACK_OK) return st;
-  DeviceInfo* d = nullptr;
-  st = device_info(&d);
-  if (st != FACK_OK) return st;
-  int tail = 0;
-  *launches = tail_split(d, M, N, K, tm, bn, sp, &tail) ? 2 : 1;
-  return FACK_OK;
 }
 
 int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,

@@ -104,14 +104,6 @@ def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     return {"libtype": "asm", "kernelName": kernel_name(tm, tn, sk), "splitK": sk, "tile_m": tm, "tile_n": tn}
 
 
-def launches(M: int, N: int, K: int, split_k: int = 0, tile_m: int = 0, tile_n: int = 0) -> int:
-    """Kernel launches one GEMM call makes (2 when a short last wave runs split first)."""
-    n = ctypes.c_int()
-    _lib.check(_lib.load().fack_gemm_bs_launches(int(M), int(N), int(K), int(tile_m), int(tile_n), int(split_k),
-                                                 ctypes.byref(n)), "fack_gemm_bs_launches")
-    return n.value
-
-
 def workspace_size(M: int, N: int, K: int, split_k: int = 0, tile_m: int = 0, tile_n: int = 0) -> int:
     """Bytes of split-K workspace for the plan (only needed with workspace="global")."""
     return plan(M, N, K, tile_m, tile_n, split_k)[3]

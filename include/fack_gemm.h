@@ -106,14 +106,6 @@ int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
                         int* tile_n, int* split_k);
 
 /*
- * Kernel launches one fack_gemm_bs / _ex call makes for this problem and
- * plan request (0 = library choice, as for fack_gemm_bs_plan): 1, or 2 when
- * an unsplit plan's last wave would hold only a few tiles -- those tiles then
- * run first in a launch of their own, split over K.  Queries the device.
- */
-int fack_gemm_bs_launches(int M, int N, int K, int tile_m, int tile_n, int split_k, int* launches);
-
-/*
  * fack_gemm_bs_ex that also stores every bf16 result to n_peers (0..7) more
  * copies of the output block, peer_outs[i] + (row * ldo + column), with the
  * same ldo: the fused compute + all-gather of the column-sharded multi-GPU
