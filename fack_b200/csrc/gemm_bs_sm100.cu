@@ -57,6 +57,7 @@ constexpr int kThreads = 384;      // 12 warps = 3 warpgroups
 constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..11 rescale and store
 constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
 constexpr int kMaxSplit = 8;       // portable cluster size
+constexpr int kSwapMaxKb = 128;    // swapped small-M tiles: K blocks per CTA whose scales fit in shared memory
 constexpr int kGroupM = 16;        // token-tile band of the grouped launch order
 constexpr int kSmemBudget = 196608;
 // Register split (setmaxnreg).  The kernel is launched with kLaunchRegs per
@@ -666,6 +667,260 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   if (p.n_peer) __threadfence_system();
 }
 
+// ------------------------------------------------------ small-M (swapped) --
+// For M <= 64 tokens the operands swap sides: a CTA owns 128 weight rows
+// (the UMMA M side, TMEM lanes) x MT tokens (the N side, MT = 16/32/64 TMEM
+// columns).  Every weight byte is then read once per K slice instead of once
+// per 128-token tile row, each TMEM accumulator is only MT columns wide -- 8
+// of them keep the MMA up to 8 K blocks ahead of the rescale -- and a K
+// slice's partial is 128 x MT fp32 (8-32 KB), so the split-K exchange is
+// small.  Per K block the scale of weight row n and token t is
+// w_scale[n0/128, kb] (one value per tile) * x_scale[t, kb]; all of them are
+// prefetched into shared memory when the CTA starts.
+template <int MT>
+struct SwapCfg {
+  static_assert(MT == 16 || MT == 32 || MT == 64, "token tile must be 16, 32 or 64");
+  static constexpr int kThreads = 192;               // warp 0 TMA, warp 1 MMA, warps 2-5 rescale
+  static constexpr int kWBytes = 128 * kBlk;         // 16 KB weight tile (UMMA A)
+  static constexpr int kXBytes = MT * kBlk;          // token tile (UMMA B)
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kStages = 6;
+  static constexpr int kBufs = 8;                    // TMEM accumulators of MT columns
+  static constexpr int kTmemCols = kBufs * MT;       // 128, 256, 512
+  static constexpr int kMaxKb = kSwapMaxKb;          // K blocks per CTA whose scales are prefetched
+  static constexpr int kPitch = 128 + 4;             // fp32 staging: one row of 128 weight rows per token
+  static constexpr int kOffW = 0;
+  static constexpr int kOffX = kStages * kWBytes;
+  static constexpr int kOffXs = kOffX + kStages * kXBytes;   // x_scale [kMaxKb][MT]
+  static constexpr int kOffWs = kOffXs + kMaxKb * MT * 4;    // w_scale [kMaxKb]
+  static constexpr int kOffBar = kOffWs + kMaxKb * 4;
+  static constexpr int kNumBars = 2 * kStages + 2 * kBufs + 1;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+  static_assert(MT * kPitch * 4 <= kOffXs, "staging must fit in the stage ring");
+  static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+template <int MT>
+__global__ void __launch_bounds__(SwapCfg<MT>::kThreads, 1)
+gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                    const __grid_constant__ Params p) {
+  using C = SwapCfg<MT>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int nt = blockIdx.x;                       // 128-row weight tile
+  const int s = blockIdx.z;                        // K slice
+  const int S = p.split;
+  const int n0 = nt * 128;
+  const int kb0 = (s * p.KB) / S;
+  const int nk = ((s + 1) * p.KB) / S - kb0;       // <= kMaxKb (checked on the host)
+  const int M = p.M;                               // <= MT
+
+  const uint32_t bar0 = base + C::kOffBar;
+  auto bar_full = [&](int i) { return bar0 + 8u * i; };
+  auto bar_empty = [&](int i) { return bar0 + 8u * (C::kStages + i); };
+  auto bar_tfull = [&](int i) { return bar0 + 8u * (2 * C::kStages + i); };
+  auto bar_tempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + C::kBufs + i); };
+  const uint32_t bar_drain = bar0 + 8u * (2 * C::kStages + 2 * C::kBufs);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+  float* xs_s = reinterpret_cast<float*>(smem + C::kOffXs);
+  float* ws_s = reinterpret_cast<float*>(smem + C::kOffWs);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(bar_full(i), 1);
+      mbar_init(bar_empty(i), 1);
+    }
+    for (int i = 0; i < C::kBufs; ++i) {
+      mbar_init(bar_tfull(i), 1);
+      mbar_init(bar_tempty(i), 4);             // one arrival per rescale warp
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dependency_wait();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint64_t tmo = p.timeout_ns;
+  unsigned int* status = &g_status;
+  int produced = 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      for (int i = 0; i < nk; ++i) {
+        const int st = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
+        if (!wait_bounded(bar_empty(st), ph ^ 1u, abort_flag, status, kStProducer, tmo)) break;
+        const int kb = kb0 + i;
+        const uint32_t sw = base + C::kOffW + st * C::kWBytes;
+        const uint32_t sx = base + C::kOffX + st * C::kXBytes;
+        mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+        if (p.w_packed)
+          tma_load_2d(sw, &tmap_w, bar_full(st), 0, (nt * p.KB + kb) * kBlk, pol_w);
+        else
+          tma_load_2d(sw, &tmap_w, bar_full(st), kb * kBlk, n0, pol_w);
+        tma_load_2d(sx, &tmap_x, bar_full(st), kb * kBlk, 0, pol_x);   // rows >= M read as zero
+        produced = i + 1;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, MT);
+      for (int i = 0; i < nk; ++i) {
+        const int st = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
+        const int buf = i % C::kBufs;
+        const uint32_t bph = (i / C::kBufs) & 1;
+        if (!wait_bounded(bar_tempty(buf), bph ^ 1u, abort_flag, status, kStMma, tmo)) break;
+        if (!wait_bounded(bar_full(st), ph, abort_flag, status, kStMma, tmo)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_kmajor_desc(base + C::kOffW + st * C::kWBytes);
+        const uint64_t db = sw128_kmajor_desc(base + C::kOffX + st * C::kXBytes);
+#pragma unroll
+        for (int k = 0; k < kBlk / 32; ++k) umma_f8(tmem_base + buf * MT, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+        umma_commit(bar_empty(st));
+        umma_commit(bar_tfull(buf));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- rescale --
+    const int et = threadIdx.x - 64;               // 0..127
+    for (int i = et; i < nk * MT; i += 128) {      // scales of this CTA's K range
+      const int kbi = i / MT, t = i % MT;
+      xs_s[i] = t < M ? p.x_scale[static_cast<int64_t>(t) * p.xs_sm + static_cast<int64_t>(kb0 + kbi) * p.xs_sk]
+                      : 0.0f;
+    }
+    for (int i = et; i < nk; i += 128) ws_s[i] = p.w_scale[static_cast<int64_t>(nt) * p.KB + kb0 + i];
+    bar_sync(1, 128);
+    const int q = warp & 3;                        // TMEM lane quarter of this warp
+    const int row = q * 32 + lane;                 // weight row inside the tile
+    float acc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) acc[t] = 0.0f;
+    bool done = true;
+    for (int i = 0; i < nk; ++i) {
+      const int buf = i % C::kBufs;
+      const uint32_t bph = (i / C::kBufs) & 1;
+      const bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
+      if (!__all_sync(0xffffffffu, got)) {
+        done = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * MT;
+      uint32_t v[MT];
+      if constexpr (MT == 16) {
+        tmem_ld16(taddr, v);
+      } else {
+#pragma unroll
+        for (int c = 0; c < MT / 32; ++c) tmem_ld32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_tempty(buf));  // the values are in registers: the buffer is free
+      const float ws = ws_s[i];
+      const float4* xs4 = reinterpret_cast<const float4*>(xs_s + i * MT);
+#pragma unroll
+      for (int t4 = 0; t4 < MT / 4; ++t4) {
+        const float4 x = xs4[t4];
+        acc[4 * t4 + 0] = fmaf(__uint_as_float(v[4 * t4 + 0]), x.x * ws, acc[4 * t4 + 0]);
+        acc[4 * t4 + 1] = fmaf(__uint_as_float(v[4 * t4 + 1]), x.y * ws, acc[4 * t4 + 1]);
+        acc[4 * t4 + 2] = fmaf(__uint_as_float(v[4 * t4 + 2]), x.z * ws, acc[4 * t4 + 2]);
+        acc[4 * t4 + 3] = fmaf(__uint_as_float(v[4 * t4 + 3]), x.w * ws, acc[4 * t4 + 3]);
+      }
+    }
+    if (done && *abort_flag == 0) {
+      // token-major staging in the idle stage ring (every stage was consumed by
+      // an MMA that completed before this warp's last wait)
+      float* stg = reinterpret_cast<float*>(smem + C::kOffW);
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+        if (t < M) stg[t * C::kPitch + row] = acc[t];
+    }
+  }
+
+  // ------------------------------------------------------------ teardown --
+  grid_launch_dependents();
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    if (*abort_flag && lane == 0) {
+      const int first = produced > C::kStages ? produced - C::kStages : 0;
+      volatile int no_abort = 0;
+      for (int i = first; i < produced; ++i)
+        wait_bounded(bar_full(i % C::kStages), (i / C::kStages) & 1, &no_abort, status, kStDrain, tmo);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      umma_commit(bar_drain);
+      volatile int no_abort = 0;
+      wait_bounded(bar_drain, 0, &no_abort, status, kStDrain, tmo);
+    }
+    __syncwarp();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  const bool ok = *abort_flag == 0;
+  const int items = M * 32;                        // 4-column chunks of the M x 128 output block
+  const float* stg = reinterpret_cast<const float*>(smem + C::kOffW);
+  if (S == 1) {
+    if (!ok) return;
+    for (int it = threadIdx.x; it < items; it += C::kThreads) {
+      const int t = it >> 5, c = (it & 31) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(stg + t * C::kPitch + c);
+      store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(v));
+    }
+    if (p.n_peer) __threadfence_system();
+    return;
+  }
+  // split-K: every CTA of the cluster reaches both barriers, also after an
+  // abort; each sums a disjoint range of the block's chunks over the slices in
+  // order 0..S-1 (bitwise reproducible)
+  cluster_sync_all();
+  if (ok) {
+    const int i0 = (s * items) / S, i1 = ((s + 1) * items) / S;
+    const uint32_t sbase = base + C::kOffW;
+    for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += C::kThreads) {
+      const int t = it >> 5, c = (it & 31) * 4;
+      const uint32_t addr = sbase + static_cast<uint32_t>((t * C::kPitch + c) * 4);
+      float4 sum = dsmem_ld4(dsmem_map(addr, 0));
+      for (int r = 1; r < S; ++r) {
+        const float4 v = dsmem_ld4(dsmem_map(addr, r));
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(sum));
+    }
+    if (p.n_peer) __threadfence_system();
+  }
+  cluster_sync_all();
+}
+
 // ------------------------------------------------------------------ prepack --
 // Tile (nb,kb) of WQ -> 16 KB block at ((nb*KB)+kb)*16384 holding the
 // 128-byte-swizzled image: byte (r,c) of the tile at r*128 + ((c/16 ^ r%8)*16) + c%16.
@@ -710,9 +965,12 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 constexpr int kMaxDevices = 64;
 
-constexpr int kVariants = 6;  // weight tiles 64, 128, 256 x (single CTA, CTA pair)
+constexpr int kVariants = 9;  // weight tiles 64, 128, 256 x (single CTA, CTA pair) + swapped 16/32/64-token tiles
 
-static int variant(int tm, int bn) { return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0); }
+static int variant(int tm, int bn) {
+  if (tm < kTileM) return 6 + (tm == 16 ? 0 : tm == 32 ? 1 : 2);
+  return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0);
+}
 
 struct DeviceInfo {
   bool init = false;
@@ -773,16 +1031,25 @@ static int device_info(DeviceInfo** out) {
 struct KernelEntry {
   const void* fn;
   int smem;
+  int threads;
+  bool split_regs;  // launched for the setmaxnreg split (exactly kLaunchRegs registers)
 };
 
 template <int BN, bool PAIR>
 static KernelEntry entry() {
-  return {reinterpret_cast<const void*>(gemm_bs_kernel<BN, PAIR>), Cfg<BN, PAIR>::kSmemBytes};
+  return {reinterpret_cast<const void*>(gemm_bs_kernel<BN, PAIR>), Cfg<BN, PAIR>::kSmemBytes, kThreads, true};
+}
+
+template <int MT>
+static KernelEntry swap_entry() {
+  return {reinterpret_cast<const void*>(gemm_bs_swap_kernel<MT>), SwapCfg<MT>::kSmemBytes, SwapCfg<MT>::kThreads,
+          false};
 }
 
 static const KernelEntry& kernel_for(int tm, int bn) {
   static const KernelEntry table[kVariants] = {entry<64, false>(), entry<128, false>(), entry<256, false>(),
-                                               entry<64, true>(),  entry<128, true>(),  entry<256, true>()};
+                                               entry<64, true>(),  entry<128, true>(),  entry<256, true>(),
+                                               swap_entry<16>(),   swap_entry<32>(),    swap_entry<64>()};
   return table[variant(tm, bn)];
 }
 
@@ -797,8 +1064,9 @@ static int ensure_configured(DeviceInfo* d, int tm, int bn) {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, k.fn);
     if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaFuncGetAttributes", e);
-    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+    if (k.split_regs && (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads))
       return fail(FACK_ERR_LAUNCH, "kernel register count differs from the setmaxnreg budget; refusing to launch");
+    if (fa.maxThreadsPerBlock < k.threads) return fail(FACK_ERR_LAUNCH, "kernel cannot run its block size");
     e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
     if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaFuncSetAttribute(max dynamic shared memory)", e);
     d->configured |= 1u << v;
@@ -817,17 +1085,17 @@ static int co_resident(DeviceInfo* d, int tm, int bn, int split) {
   }
   if (ensure_configured(d, tm, bn) != FACK_OK) return 0;
   const KernelEntry& k = kernel_for(tm, bn);
-  const int cx = tm / kTileM;  // pairs along cluster x
+  const int cx = tm == 256 ? 2 : 1;  // pairs along cluster x
   int n = 0;
   if (split == 1 && cx == 1) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kThreads, k.smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, k.threads, k.smem) != cudaSuccess) return 0;
     n = per_sm * d->sms;
   } else {
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(cx, 1, split);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(k.threads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -848,6 +1116,12 @@ static int co_resident(DeviceInfo* d, int tm, int bn, int split) {
 // valid token) so that the pair lies along the cluster's x dimension,
 // y = weight tiles.  z = K slices.
 static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, int* gz) {
+  if (tm < kTileM) {  // swapped small-M tiles: x = 128-row weight tiles
+    *gx = N / kBlk;
+    *gy = 1;
+    *gz = sp;
+    return;
+  }
   if (tm == 256) {
     *gx = 2 * ((M + 255) / 256);
     *gy = N / bn;
@@ -874,6 +1148,21 @@ static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, in
 // time of the operands.
 static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int sp) {
   const int KB = K / kBlk;
+  if (tm < kTileM) {
+    // swapped small-M tiles: 128 weight rows x tm tokens; eight TMEM buffers
+    // hide the rescale, so a K block costs the fill (weight tile + token
+    // tile) or the narrow MMA (~226 cycles), whichever is slower
+    const int tiles = N / kBlk;
+    const int slots = co_resident(d, tm, kBlk, sp);
+    if (slots <= 0) return 1e30;
+    const int waves = (tiles + slots - 1) / slots;
+    const int steps = (KB + sp - 1) / sp;
+    const double t_kb = fmax((128.0 * 128.0 + tm * 128.0) / 44.0, 226.0);
+    const double out = sp > 1 ? tm * 128.0 * 4.0 * (sp - 1) / sp / 18.0 + 2500.0 : M * 128.0 * 2.0 / 24.0;
+    const double cyc = static_cast<double>(waves) * (steps * t_kb + 4000.0 + out);
+    const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K;
+    return fmax(cyc, bytes / 6.5e12 * 1.9e9);
+  }
   const int tiles = (N / bn) * ((M + tm - 1) / tm) * (tm / kTileM);   // CTAs per K slice
   const int slots = co_resident(d, tm, bn, sp) * (tm / kTileM);       // CTAs per K slice resident at once
   if (slots <= 0) return 1e30;
@@ -895,6 +1184,11 @@ static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int 
 // token tiles unless pairs are requested, then the largest weight tile that
 // still gives >= 120 CTAs, else the smallest.
 static void tiles_for_split(int M, int N, int sp, int tm_req, int bn_req, int* tm, int* bn) {
+  if (tm_req && tm_req < kTileM) {  // swapped small-M tiles always span 128 weight rows
+    *tm = tm_req;
+    *bn = kBlk;
+    return;
+  }
   int t = tm_req ? tm_req : 128;
   int b = bn_req;
   if (!b) {
@@ -924,6 +1218,22 @@ static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req,
   int bt = 0, bb = 0, bs = 0;
   // CTA pairs are chosen only on request for now: their cross-CTA handshakes
   // currently cost more per K block than the weight bytes they save.
+  // swapped small-M tiles: the requested one, else the smallest token tile
+  // that holds all M tokens
+  const int tm_swap = tm_req && tm_req < kTileM ? tm_req : tm_req ? 0 : M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
+  if (tm_swap && M <= tm_swap && (bn_req == 0 || bn_req == kBlk)) {
+    for (int sp = 1; sp <= KB && sp <= kMaxSplit; ++sp) {
+      if ((KB + sp - 1) / sp > kSwapMaxKb) continue;
+      if (sp > 1 && KB / sp < 2) break;
+      const double c = plan_cost(d, M, N, K, tm_swap, kBlk, sp);
+      if (c < best * 0.97) {
+        best = c;
+        bt = tm_swap;
+        bb = kBlk;
+        bs = sp;
+      }
+    }
+  }
   for (int tm : {128, 256}) {
     if (tm_req ? tm != tm_req : tm != 128) continue;
     for (int bn : {256, 128, 64}) {
@@ -949,7 +1259,7 @@ static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req,
 }
 
 static size_t workspace_bytes_for(int M, int N, int tm, int bn, int split) {
-  if (split <= 1) return 0;
+  if (split <= 1 || tm < kTileM) return 0;  // swapped tiles combine through distributed shared memory only
   int gx, gy, gz;
   plan_grid(M, N, tm, bn, split, &gx, &gy, &gz);
   return static_cast<size_t>(gx) * gy * split * kTileM * bn * sizeof(float);
@@ -978,7 +1288,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(gx, gy, gz);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(k.threads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -991,7 +1301,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   ++cfg.numAttrs;
   if (p.split > 1 || tm == 256) {
     attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-    attr[cfg.numAttrs].val.clusterDim.x = tm / kTileM;  // CTA pairs lie along cluster x
+    attr[cfg.numAttrs].val.clusterDim.x = tm == 256 ? 2 : 1;  // CTA pairs lie along cluster x
     attr[cfg.numAttrs].val.clusterDim.y = 1;
     attr[cfg.numAttrs].val.clusterDim.z = p.split;
     ++cfg.numAttrs;
@@ -1065,7 +1375,13 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
   if (!tile_m || !tile_n || !split_k) return FACK_ERR_BAD_ARG;
   const int KB = K / kBlk;
   if (split_k_request < 0 || split_k_request > kMaxSplit || split_k_request > KB) return FACK_ERR_BAD_ARG;
-  if (tile_m_request != 0 && tile_m_request != 128 && tile_m_request != 256) return FACK_ERR_BAD_ARG;
+  if (tile_m_request != 0 && tile_m_request != 16 && tile_m_request != 32 && tile_m_request != 64 &&
+      tile_m_request != 128 && tile_m_request != 256)
+    return FACK_ERR_BAD_ARG;
+  if (tile_m_request && tile_m_request < kTileM) {  // swapped small-M tiles
+    if (M > tile_m_request || (tile_n_request && tile_n_request != kBlk)) return FACK_ERR_BAD_ARG;
+    if (split_k_request && (KB + split_k_request - 1) / split_k_request > kSwapMaxKb) return FACK_ERR_BAD_ARG;
+  }
   if (tile_n_request != 0 && tile_n_request != 64 && tile_n_request != 128 && tile_n_request != 256)
     return FACK_ERR_BAD_ARG;
   if (tile_n_request && N % tile_n_request) return FACK_ERR_BAD_ARG;
@@ -1166,7 +1482,7 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   else
     st = encode_2d(&tw, wq, K, N, K, kBlk, wrows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
-  st = encode_2d(&tx, xq, K, M, ldx, kBlk, kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
+  st = encode_2d(&tx, xq, K, M, ldx, kBlk, tm < kTileM ? tm : kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FACK_OK) return st;
 
   Params p;

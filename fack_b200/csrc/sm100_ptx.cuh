@@ -355,6 +355,11 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Named barrier over `count` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Named barrier over `count` threads that also ANDs a predicate across them:
 // every participant gets the same answer, so a group of warps can leave a
 // loop together and none is left waiting at the next barrier.

@@ -12,7 +12,7 @@
 // CSV form read by fack_gemm_bs_tuned_load: '#' lines are comments; the first
 // other line is a header; columns are found by name, so order and extra
 // columns do not matter.  Required: cu_num, M, N, K, kernelName (this
-// library's fack_bs_sm100_t{128|256}x{64|128|256}_s{S}).  Optional: splitK
+// library's fack_bs_sm100_t{16|32|64|128|256}x{64|128|256}_s{S}).  Optional: splitK
 // (must equal the name's S) and errRatio (must be 0).  Rows naming another
 // library's kernel (a gfx942 symbol) are skipped and counted.  The file is
 // checked whole before any row is added: a bad row leaves the table as it was.
@@ -98,6 +98,12 @@ bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp) {
 
 int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
   if (M < 1 || N < 128 || K < 128 || N % 128 || K % 128 || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
+  if (tile_m == 16 || tile_m == 32 || tile_m == 64) {  // swapped small-M tiles: 128 weight rows, all M tokens
+    if (M > tile_m || tile_n != 128 || split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128 ||
+        (K / 128 + split_k - 1) / split_k > 128)
+      return FACK_ERR_BAD_ARG;
+    return FACK_OK;
+  }
   if (tile_m != 128 && tile_m != 256) return FACK_ERR_BAD_ARG;
   if ((tile_n != 64 && tile_n != 128 && tile_n != 256) || N % tile_n) return FACK_ERR_BAD_ARG;
   if (split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128) return FACK_ERR_BAD_ARG;

@@ -9,9 +9,11 @@ namespace fack {
 constexpr int kTunedMaxSplit = 8;  // the GEMM's cluster limit along K
 
 // Checks a fully specified plan against the kernel's rules: M >= 1, N and K
-// positive multiples of 128; tile_m 128 (one CTA) or 256 (a CTA pair);
-// tile_n 64, 128 or 256 dividing N; 1 <= split_k <= min(8, K/128), and
-// 2 * split_k <= 8 for a pair.  Returns a FACK_* status.
+// positive multiples of 128; tile_m 128 (one CTA) or 256 (a CTA pair) with
+// tile_n 64, 128 or 256 dividing N, 1 <= split_k <= min(8, K/128), and
+// 2 * split_k <= 8 for a pair; or tile_m 16, 32, 64 (swapped small-M tiles,
+// M <= tile_m) with tile_n 128 and at most 128 K blocks per slice.  Returns a
+// FACK_* status.
 int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k);
 
 // The row for (cu_num, M, N, K), if any.  Thread-safe.

@@ -82,8 +82,8 @@ def parse_kernel_name(name) -> tuple:
     applies here, so they (and None / "") leave the choice to the library."""
     if not name or name in AITER_SYMBOLS:
         return 0, 0, 0
-    m = re.fullmatch(KERNEL_PREFIX + r"_t(128|256)x(64|128|256)_s([1-8])", str(name))
-    if not m or (m.group(1) == "256" and int(m.group(3)) > 4):
+    m = re.fullmatch(KERNEL_PREFIX + r"_t(16|32|64|128|256)x(64|128|256)_s([1-8])", str(name))
+    if not m or (m.group(1) == "256" and int(m.group(3)) > 4) or (int(m.group(1)) < 128 and m.group(2) != "128"):
         raise ValueError(f"unknown blockscale kernel {name!r}")
     return int(m.group(1)), int(m.group(2)), int(m.group(3))
 

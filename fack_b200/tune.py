@@ -4,7 +4,8 @@
 
 For every (M, N, K) the tuner times each valid plan of the kernel --
 token tile 128 (one CTA) or 256 (a CTA pair), weight tile 64, 128 or 256
-dividing N, split-K 1..min(8, K/128) (pairs: 1..4) -- through the same entry
+dividing N, split-K 1..min(8, K/128) (pairs: 1..4), and for M <= 64 the
+swapped 16/32/64-token tiles -- through the same entry
 the reference calls (pre-packed weight, transposed x_scale, split-K slices
 combined in distributed shared memory), checks each plan's output against an
 fp32 dequantise-then-matmul on the device, and writes the fastest plan per
@@ -79,6 +80,9 @@ def candidates(M: int, N: int, K: int) -> list:
     """Every (tile_m, tile_n, split_k) the planner accepts for the shape."""
     KB = K // ops.BLOCK
     plans = []
+    for tm in (16, 32, 64):                      # swapped small-M tiles hold all M tokens
+        if M <= tm:
+            plans += [(tm, 128, sk) for sk in range(1, min(8, KB) + 1) if -(-KB // sk) <= 128]
     for tm in (128, 256):
         for tn in (256, 128, 64):
             if N % tn:

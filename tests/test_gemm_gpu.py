@@ -60,11 +60,13 @@ def test_golden_every_tile_and_split(cuda_device, name, packed):
     tile kernels) at every split-K the shape allows."""
     g = golden_on(name, cuda_device)
     b = fb.shuffle_weight(g["b"]) if packed else g["b"]
-    for tile_m in (128, 256):                      # 256 = a CTA pair sharing each MMA
+    for tile_m in (16, 32, 64, 128, 256):          # 256 = a CTA pair; 16-64 = swapped small-M tiles
+        if tile_m < 128 and g["m"] > tile_m:
+            continue
         for tile in (64, 128, 256):
-            if g["n"] % tile:
+            if g["n"] % tile or (tile_m < 128 and tile != 128):
                 continue
-            for split in range(1, min(8 if tile_m == 128 else 4, g["k"] // 128) + 1):
+            for split in range(1, min(8 if tile_m != 256 else 4, g["k"] // 128) + 1):
                 out = poisoned(g["m"], g["n"], cuda_device)
                 fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=split,
                                                         kernelName=f"fack_bs_sm100_t{tile_m}x{tile}_s{split}",
@@ -106,6 +108,38 @@ def test_decode_sweep_vs_oracle(cuda_device, decode_weights, m):
     fb.gemm_a8w8_blockscale_bpreshuffle_asm(xq.to(d), fb.shuffle_weight(wq.to(d)), out,
                                             data.to_aiter_xscale(xs).to(d), ws.to(d), splitK=None)
     assert_close(out, ref, f"M={m}")
+
+
+@pytest.mark.parametrize("m", [1, 7, 16, 17, 32, 33, 64])
+def test_small_m_swapped_tiles_vs_oracle(cuda_device, decode_weights, m):
+    """Swapped small-M tiles (128 weight rows x 16/32/64 tokens) at N=3072,
+    K=7168: the library's plan, and explicit token tiles and splits."""
+    wq, ws = decode_weights
+    xq, xs = data.make_activations(m, 7168, "normal", seed=300 + m)
+    ref = orc.reference_gemm(xq, wq, xs, ws)
+    d = cuda_device
+    packed = fb.shuffle_weight(wq.to(d))
+    xq_d, sa_d, ws_d = xq.to(d), data.to_aiter_xscale(xs).to(d), ws.to(d)
+    from fack_b200 import _lib
+    lib = _lib.load()
+    lib.fack_gemm_bs_tuned_clear()                       # the cost model's own choice ...
+    try:
+        cfg = fb.get_config(m, 3072, 7168)
+    finally:
+        for table in _lib.tuned_tables():
+            _lib.load_tuned(table, lib)
+    assert cfg["tile_m"] < 128, cfg                      # ... is a swapped tile here
+    plans = [(None, None)] + [(t, s) for t in (16, 32, 64) if t >= m for s in (1, 3, 6, 8)]
+    for tile_m, split in plans:
+        out = poisoned(m, 3072, d)
+        name = None if tile_m is None else f"fack_bs_sm100_t{tile_m}x128_s{split}"
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(xq_d, packed, out, sa_d, ws_d, splitK=split, kernelName=name)
+        assert_close(out, ref, f"M={m} {name or cfg['kernelName']}")
+    # split-K over the cluster is bitwise reproducible; row-major weights give the same bits
+    first = fb.gemm_blockscale(xq_d, wq.to(d), xs.to(d), ws_d, split_k=6, tile_m=32 if m <= 32 else 64)
+    for _ in range(3):
+        again = fb.gemm_blockscale(xq_d, packed, xs.to(d), ws_d, split_k=6, tile_m=32 if m <= 32 else 64)
+        assert torch.equal(again.view(torch.int16), first.view(torch.int16))
 
 
 def test_plumbing_shape_vs_oracle(cuda_device):

@@ -63,7 +63,8 @@ def test_kernel_name_round_trip():
     assert ops.parse_kernel_name(ops.kernel_name(256, 64, 4)) == (256, 64, 4)
     assert ops.parse_kernel_name(None) == (0, 0, 0)
     assert ops.parse_kernel_name("_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_96x128E") == (0, 0, 0)
+    assert ops.parse_kernel_name(ops.kernel_name(16, 128, 6)) == (16, 128, 6)   # swapped small-M tile
     for bad in ("fack_bs_sm100_t128x96_s2", "fack_bs_sm100_t128x128_s9", "fack_bs_sm100_t256x128_s6",
-                "fack_bs_sm100_t64x128_s1"):
+                "fack_bs_sm100_t64x256_s1", "fack_bs_sm100_t48x128_s1"):
         with pytest.raises(ValueError):
             ops.parse_kernel_name(bad)

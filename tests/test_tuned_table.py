@@ -126,14 +126,15 @@ def test_environment_tables_merge_over_the_shipped_one(tmp_path):
 def test_tuner_candidates_are_exactly_the_valid_plans():
     lib = _lib.load()
     tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
-    for M, N, K in ((256, 3072, 7168), (48, 4096, 2048), (33, 384, 640), (1, 128, 256)):
+    for M, N, K in ((256, 3072, 7168), (48, 4096, 2048), (33, 384, 640), (1, 128, 256), (16, 3072, 7168),
+                    (64, 1024, 40960)):
         cands = tune.candidates(M, N, K)
         assert len(set(cands)) == len(cands)
         for c in cands:
             assert lib.fack_gemm_bs_plan(M, N, K, *c, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
                                          ctypes.byref(nb)) == 0
             assert (tm.value, tn.value, sk.value) == c
-        for t_m in (128, 256):
+        for t_m in (16, 32, 64, 128, 256):
             for t_n in (64, 128, 256):
                 for s in range(1, 9):
                     ok = lib.fack_gemm_bs_plan(M, N, K, t_m, t_n, s, ctypes.byref(tm), ctypes.byref(tn),
