@@ -78,8 +78,11 @@ const char* fack_last_error(void);
 /*
  * Full plan for an (M,N,K) problem: the token tile (128 = one CTA per tile;
  * 256 = a pair of CTAs sharing each tensor-core MMA through a 2-SM cluster,
- * each loading half of the weight rows), the weight-tile width (64, 128 or
- * 256), split-K (1..8; 2 x split <= 8 for pairs) -- 0 for any of them = the
+ * each loading half of the weight rows; 16, 32 or 64 = swapped small-M tiles
+ * for M <= the tile: 128 weight rows on the MMA's M side x all M tokens on its
+ * N side, weight tile 128, at most 128 K blocks per slice, split-K always
+ * through distributed shared memory, no workspace), the weight-tile width
+ * (64, 128 or 256), split-K (1..8; 2 x split <= 8 for pairs) -- 0 for any of them = the
  * library's choice -- and the workspace bytes fack_gemm_bs_ex needs for that
  * plan when the caller supplies a workspace (0 for a single K slice).  A
  * library choice of split-K queries the current device (cluster occupancy); an
