@@ -158,6 +158,43 @@ def test_sibling_gemm_validation_before_device():
     assert plan(BF, M, N, 1024, 256, 64, 5)[0] == _lib.FACK_ERR_BAD_ARG
 
 
+def test_swapped_tiles_peer_outputs_and_ipc_validation_before_device():
+    lib = _lib.load()
+    ok = 1 << 20  # fake 16-byte aligned address: every call below fails validation first
+    tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+
+    def plan(M, N, K, m=0, n=0, s=0):
+        st = lib.fack_gemm_bs_plan(M, N, K, m, n, s, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
+                                   ctypes.byref(nb))
+        return st, tm.value, tn.value, sk.value, nb.value
+
+    # swapped small-M tiles: all M tokens in one tile, 128 weight rows, no workspace
+    assert plan(16, 3072, 7168, m=16, s=5) == (0, 16, 128, 5, 0)
+    assert plan(33, 3072, 7168, m=64, n=128, s=8) == (0, 64, 128, 8, 0)
+    assert plan(17, 3072, 7168, m=16, s=5)[0] == _lib.FACK_ERR_BAD_ARG       # 17 tokens do not fit 16
+    assert plan(16, 3072, 7168, m=16, n=256, s=5)[0] == _lib.FACK_ERR_BAD_ARG  # weight tile is 128
+    assert plan(16, 3072, 131072, m=16, s=1)[0] == _lib.FACK_ERR_BAD_ARG      # 1024 K blocks > 128 per slice
+    assert plan(16, 3072, 7168, m=48, s=1)[0] == _lib.FACK_ERR_BAD_ARG        # not a tile size
+    # peer outputs of the fused multi-GPU path
+    M, N, K = 32, 256, 512
+    peers8 = (ctypes.c_void_p * 8)(*([ok] * 8))
+    peers_bad = (ctypes.c_void_p * 2)(ok, ok + 8)
+
+    def bcast(peers, n):
+        return lib.fack_gemm_bs_bcast(ok, K, ok, 0, ok, 1, 1, ok, ok, N, peers, n, M, N, K, 0, 0, 1, None, 0, None)
+
+    assert bcast(peers8, 8) == _lib.FACK_ERR_BAD_ARG                      # at most 7 peers
+    assert bcast(None, 1) == _lib.FACK_ERR_BAD_ARG
+    assert bcast(peers_bad, 2) == _lib.FACK_ERR_BAD_ALIGN
+    assert bcast(peers8, -1) == _lib.FACK_ERR_BAD_ARG
+    # CUDA IPC entry points reject missing arguments before any CUDA call
+    off = ctypes.c_size_t()
+    assert lib.fack_ipc_get_handle(None, ctypes.create_string_buffer(64), 64, ctypes.byref(off)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_ipc_get_handle(ok, ctypes.create_string_buffer(64), 32, ctypes.byref(off)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_ipc_open_handle(None, ctypes.byref(ctypes.c_void_p())) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_ipc_close_handle(None) == _lib.FACK_ERR_BAD_ARG
+
+
 def test_check_maps_contract_violations_to_valueerror():
     with pytest.raises(ValueError):
         _lib.check(_lib.FACK_ERR_BAD_SHAPE, "x")
