@@ -447,46 +447,72 @@ def run_e2e(args, wl, s0, dev, stream, sharder, world):
             y = fb.gemm_a8w8_blockscale_bpreshuffle(a_d, s0["b"], sa_d, s0["sb"], dtype=torch.bfloat16)
         y_h.copy_(y, non_blocking=True)
 
-    # Unsharded: each step's copy-in, GEMM and copy-out on three streams over two
+    # Unsharded: each step's copy-in, call and copy-out on three streams over two
     # device buffers, so step i's inputs cross PCIe while step i-1 computes and
-    # step i-2's result comes back (each step still moves its own bytes).  The
-    # sharded call holds collectives on its stream and stays sequential.
+    # step i-2's result comes back (each step still moves its own bytes); the
+    # steps are captured in CUDA graphs of `per_graph` steps, as the
+    # reference's runner captures its timed launches (client/aiter/runner.py:
+    # 169-172), so host-side Python does not pace the pipeline.  The call is the
+    # reference's timed operator, gemm_a8w8_blockscale_bpreshuffle_asm, with a
+    # caller-owned output and the plan the public entry selects.  The sharded
+    # call holds collectives on its stream and stays sequential.
     pipelined = sharder is None
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if pipelined:
+        cfg = fb.get_config(wl.M, wl.N, wl.K)
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         a_b = [a_d, torch.empty_like(a_d)]
         sa_b = [sa_d, torch.empty_like(sa_d)]
+        out_b = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
         y_hb = [y_h, torch.empty_like(y_h).pin_memory()]
         ev_in = [torch.cuda.Event(), torch.cuda.Event()]
         ev_comp = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_out = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_fork = torch.cuda.Event()
 
-        def one_pipelined(i):
-            b = i % 2
-            with torch.cuda.stream(s_in):
-                s_in.wait_event(ev_comp[b])            # step i-2's GEMM has read these buffers
-                a_b[b].copy_(a_h, non_blocking=True)
-                sa_b[b].copy_(sa_h, non_blocking=True)
-                ev_in[b].record(s_in)
-            stream.wait_event(ev_in[b])
-            with torch.cuda.stream(stream):
-                y = fb.gemm_a8w8_blockscale_bpreshuffle(a_b[b], s0["b"], sa_b[b], s0["sb"], dtype=torch.bfloat16)
-                y.record_stream(s_out)                 # not reused before its copy-out
+        def steps_graph(n):
+            ev_fork.record(stream)                     # the side streams join the capture here
+            s_in.wait_event(ev_fork)
+            s_out.wait_event(ev_fork)
+            for i in range(n):
+                b = i % 2
+                if i >= 2:
+                    s_in.wait_event(ev_comp[b])        # step i-2's call has read these inputs
+                with torch.cuda.stream(s_in):
+                    a_b[b].copy_(a_h, non_blocking=True)
+                    sa_b[b].copy_(sa_h, non_blocking=True)
+                    ev_in[b].record(s_in)
+                stream.wait_event(ev_in[b])
+                if i >= 2:
+                    stream.wait_event(ev_out[b])       # step i-2's result has left out_b[b]
+                fb.gemm_a8w8_blockscale_bpreshuffle_asm(a_b[b], s0["b"], out_b[b], sa_b[b], s0["sb"], None,
+                                                        cfg["splitK"], cfg["kernelName"], True)
                 ev_comp[b].record(stream)
-            s_out.wait_event(ev_comp[b])
-            with torch.cuda.stream(s_out):
-                y_hb[b].copy_(y, non_blocking=True)
+                s_out.wait_event(ev_comp[b])
+                with torch.cuda.stream(s_out):
+                    y_hb[b].copy_(out_b[b], non_blocking=True)
+                    ev_out[b].record(s_out)
+            stream.wait_event(ev_out[(n - 1) % 2])    # join both side streams back
+            stream.wait_event(ev_in[(n - 1) % 2])
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if pipelined:
-        for i in range(4):
-            one_pipelined(i)
-        torch.cuda.synchronize(dev)
-        barrier(world)
-        start.record(s_in)
-        for i in range(steps):
-            one_pipelined(i)
-        end.record(s_out)                              # after the last copy-out, which follows every step
-        end.synchronize()
+        per_graph = min(steps, 64)
+        with torch.cuda.stream(stream):
+            steps_graph(2)                             # eager warm-up outside capture
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                steps_graph(per_graph)
+            g.replay()                                 # warm replay
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            reps = max(1, steps // per_graph)
+            start.record(stream)
+            for _ in range(reps):
+                g.replay()
+            end.record(stream)
+            end.synchronize()
+        g.reset()
+        steps = reps * per_graph
     else:
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -503,9 +529,10 @@ def run_e2e(args, wl, s0, dev, stream, sharder, world):
     return {"value": round(work / (ms / 1e3) / 1e12, 4), "unit": "TFLOPS",
             "h2d_bytes_per_step": a_h.numel() * a_h.element_size() + sa_h.numel() * 4,
             "d2h_bytes_per_step": y_h.numel() * 2, "steps": steps, "us_per_step": round(ms * 1e3 / steps, 2),
-            "api": "fack_b200.gemm_a8w8_blockscale_bpreshuffle (public entry, allocates out, selects kernel)"
-                   + ("; per step: pinned copy-in, call, copy-out on three streams over two buffers"
-                      if pipelined else "; per step: copy-in, sharded call, copy-out on one stream")}
+            "api": ("fack_b200.gemm_a8w8_blockscale_bpreshuffle_asm with the plan of get_config; per step: pinned "
+                    "copy-in, call, copy-out on three streams over two buffers, CUDA graphs of 64 steps"
+                    if pipelined else "fack_b200.dist.ShardedBlockscaleGemm; per step: copy-in, sharded call, "
+                    "copy-out on one stream")}
 
 
 # ------------------------------------------------------- reference arm --
