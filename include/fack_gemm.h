@@ -234,11 +234,11 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * fack_gemm_bs without a workspace argument, for callers that cannot allocate
- * device memory when they call the GEMM: an engine plugin whose enqueue path
- * must neither allocate nor synchronise (cudaMalloc may synchronise the
- * device), code that runs inside a CUDA stream capture, or a process whose
- * device memory is wholly owned by another allocator.  No counterpart in the
+ * fack_gemm_bs without a workspace argument, for callers that cannot call
+ * cudaMalloc when they run the GEMM: an engine plugin whose enqueue path must
+ * neither allocate nor synchronise (cudaMalloc may synchronise the device), or
+ * a process whose device memory is wholly owned by another allocator with a
+ * fixed budget.  No counterpart in the
  * reference (aiter's launcher allocates its own buffers).
  *
  * The split-K partial sums go to one 16 MiB buffer compiled into this library
