@@ -1,8 +1,8 @@
 """GPU: the no-allocation entry point, fack_gemm_bs_noalloc.
 
-Some callers cannot allocate device memory at the moment they run the GEMM (a
-plugin's enqueue path that must not allocate or synchronise, code inside a
-CUDA stream capture, a process whose memory another allocator owns).  For them
+Some callers cannot call cudaMalloc at the moment they run the GEMM (a plugin's
+enqueue path that must not allocate or synchronise, a process whose device
+memory another allocator owns).  For them
 the library keeps its split-K scratch in a fixed 16 MiB buffer compiled into
 the library.  These tests call that entry point through the C ABI and check
 it against the regular entry point with a caller-owned workspace, twice in a
