@@ -360,22 +360,6 @@ __device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Named barrier over `count` threads that also ANDs a predicate across them:
-// every participant gets the same answer, so a group of warps can leave a
-// loop together and none is left waiting at the next barrier.
-__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return out != 0;
-}
-
 // ---------------------------------------------- distributed shared memory --
 // Address of the same shared-memory location in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t dsmem_map(uint32_t local, uint32_t rank) {
