@@ -1155,7 +1155,10 @@ static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int 
     const int tiles = N / kBlk;
     const int slots = co_resident(d, tm, kBlk, sp);
     if (slots <= 0) return 1e30;
-    const int waves = (tiles + slots - 1) / slots;
+    // one wave only: with more weight tiles than co-resident CTAs (a wide
+    // layer) the 128 x 256 tiles of the regular kernel measure faster
+    if (tiles * sp > slots) return 1e30;
+    const int waves = 1;
     const int steps = (KB + sp - 1) / sp;
     const double t_kb = fmax((128.0 * 128.0 + tm * 128.0) / 44.0, 226.0);
     const double out = sp > 1 ? tm * 128.0 * 4.0 * (sp - 1) / sp / 18.0 + 2500.0 : M * 128.0 * 2.0 / 24.0;
