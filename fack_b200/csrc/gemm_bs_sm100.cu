@@ -1153,11 +1153,11 @@ static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int 
     // hide the rescale, so a K block costs the fill (weight tile + token
     // tile) or the narrow MMA (~226 cycles), whichever is slower
     const int tiles = N / kBlk;
-    const int slots = co_resident(d, tm, kBlk, sp);
+    const int slots = co_resident(d, tm, kBlk, sp);                 // clusters of sp K slices
     if (slots <= 0) return 1e30;
-    // one wave only: with more weight tiles than co-resident CTAs (a wide
-    // layer) the 128 x 256 tiles of the regular kernel measure faster
-    if (tiles * sp > slots) return 1e30;
+    // one wave only: with more weight tiles than co-resident clusters (a
+    // wide layer) the 128 x 256 tiles of the regular kernel measure faster
+    if (tiles > slots) return 1e30;
     const int waves = 1;
     const int steps = (KB + sp - 1) / sp;
     const double t_kb = fmax((128.0 * 128.0 + tm * 128.0) / 44.0, 226.0);
