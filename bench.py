@@ -365,7 +365,13 @@ def run_ours(args):
     else:
         roof = {"bound": "tensor", "achieved": round(tflops_k, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
                 "frac": round(tflops_k / fp8_peak, 4)}
-    roof.update({"traffic": load_traffic(args.workload), "algorithmic_bytes": k_bytes,
+    # ncu DRAM bytes of the workload's single-GPU launch; a column shard reads
+    # its share of the weights (they are all but ~1 % of the bytes), so its
+    # launch is scaled by n_local / N
+    traffic = load_traffic(args.workload)
+    if traffic is not None and sharded:
+        traffic = int(round(traffic * n_local / wl.N))
+    roof.update({"traffic": traffic, "algorithmic_bytes": k_bytes,
                  "kernel_us": round(k_us, 3), "peak_source": (
                      f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 "
                      f"{'sustained' if sustained else 'burst'} {bf16_peak} TFLOP/s ({why})"),
