@@ -14,6 +14,7 @@ from .ops import (  # noqa: F401
     gather_interleave,
     gemm_a8w8_blockscale_bpreshuffle,
     gemm_a8w8_blockscale_bpreshuffle_asm,
+    gemm_a8w8_blockscale_bpreshuffle_ck,
     gemm_blockscale,
     get_config,
     quantize_activations,
@@ -31,6 +32,7 @@ __all__ = [
     "gemm_tn",
     "gemm_a8w8_blockscale_bpreshuffle",
     "gemm_a8w8_blockscale_bpreshuffle_asm",
+    "gemm_a8w8_blockscale_bpreshuffle_ck",
     "gemm_blockscale",
     "get_config",
     "quantize_activations",

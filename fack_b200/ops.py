@@ -10,6 +10,9 @@ Two layers:
     zero_bias_buf=None)`` -- the low-level operator the reference times
     (client/aiter/hsa/gfx942/driver.py:26-29; signature observed at
     client/aiter/hsa/gfx942/dispatch_driver.py:62-63);
+  - ``gemm_a8w8_blockscale_bpreshuffle_ck(x, weight, x_scale, w_scale, out,
+    kernelName="")`` -- the CK sibling the reference's op_test tier checks
+    the asm operator against (client/aiter/hsa/gfx942/optest_driver.py:79-81);
   - ``gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale,
     dtype=torch.bfloat16)`` -- the public entry that picks the kernel and
     split-K itself and allocates ``out``
@@ -243,6 +246,27 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     sm, sk = _aiter_xscale_strides(x_scale, M, K // BLOCK)
     split = name_split if splitK is None else int(splitK)
     return _launch(a, b, shuffled, x_scale, sm, sk, w_scale, out, split, tile_m, tile_n)
+
+
+def gemm_a8w8_blockscale_bpreshuffle_ck(x, weight, x_scale, w_scale, out, kernelName=""):
+    """Drop-in for aiter's CK sibling ``gemm_a8w8_blockscale_bpreshuffle_ck``,
+    the independent implementation the reference's op_test tier compares the
+    asm operator with (client/aiter/hsa/gfx942/optest_driver.py:79-81).
+
+    Same operands and ``x_scale`` convention as
+    :func:`gemm_a8w8_blockscale_bpreshuffle_asm`; writes and returns ``out``;
+    no split-K argument.  The weight must be a :func:`shuffle_weight` output
+    (the operator is the pre-shuffled one).  ``kernelName`` "" (CK's default
+    instance, the one op_test pins) lets the library choose the plan; one of
+    this library's ``fack_bs_sm100_...`` names fixes it; CK instance names
+    and the gfx942 asm symbols are refused.
+    """
+    if kernelName and (kernelName in AITER_SYMBOLS or not str(kernelName).startswith(KERNEL_PREFIX)):
+        raise ValueError(f"unknown blockscale CK kernel {kernelName!r}")
+    if not getattr(weight, "is_shuffled", False):
+        raise ValueError("the pre-shuffled CK operator takes a shuffle_weight() output")
+    return gemm_a8w8_blockscale_bpreshuffle_asm(x, weight, out, x_scale, w_scale, None, None,
+                                                kernelName or None, True)
 
 
 def gemm_a8w8_blockscale_bpreshuffle(x, weight, x_scale, w_scale, dtype=torch.bfloat16):

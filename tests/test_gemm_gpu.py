@@ -91,6 +91,23 @@ def test_golden_public_dispatch_and_native_layout(cuda_device, name):
     assert cfg["kernelName"].startswith("fack_bs_sm100_t") and cfg["splitK"] >= 1
 
 
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_ck_sibling(cuda_device, name):
+    """The CK sibling (optest_driver.py:79-81): kernelName "" and the
+    transposed x_scale as a contiguous view or as its strided (1, M) view give
+    the asm operator's bits."""
+    g = golden_on(name, cuda_device)
+    packed_b = fb.shuffle_weight(g["b"])
+    want = fb.gemm_a8w8_blockscale_bpreshuffle(g["a"], packed_b, g["packed_sa"], g["sb"])
+    strided_sa = g["packed_sa"].view(-1).view(g["k"] // 128, g["m"]).t()
+    for sa in (g["packed_sa"], strided_sa):
+        out = poisoned(g["m"], g["n"], cuda_device)
+        r = fb.gemm_a8w8_blockscale_bpreshuffle_ck(g["a"], packed_b, sa, g["sb"], out, kernelName="")
+        assert r is out
+        assert_close(out, g["reference"], name + " ck")
+        assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+
+
 @pytest.fixture(scope="module")
 def decode_weights():
     wl = data.WORKLOADS["decode"]

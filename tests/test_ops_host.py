@@ -68,3 +68,15 @@ def test_kernel_name_round_trip():
                 "fack_bs_sm100_t64x256_s1", "fack_bs_sm100_t48x128_s1"):
         with pytest.raises(ValueError):
             ops.parse_kernel_name(bad)
+
+
+def test_ck_sibling_contract():
+    """gemm_a8w8_blockscale_bpreshuffle_ck (optest_driver.py:79-81): CK
+    instance names and asm symbols are refused, and the weight must be
+    pre-shuffled, before anything launches."""
+    a, b, out, xs, ws = cpu_case()
+    for bad in ("some_ck_instance", "_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_32x128E"):
+        with pytest.raises(ValueError, match="CK kernel"):
+            fb.gemm_a8w8_blockscale_bpreshuffle_ck(a, b, xs, ws, out, kernelName=bad)
+    with pytest.raises(ValueError, match="shuffle_weight"):
+        fb.gemm_a8w8_blockscale_bpreshuffle_ck(a, b, xs, ws, out)
