@@ -554,12 +554,20 @@ def run_reference(args):
     xq, xs = data.make_activations(wl.M, wl.K, wl.x_dist, seed=0)
     # size the per-step column sample so warm-up + steps fit the time budget
     wq, ws = data.make_weights(128, wl.K, "normal" if wl.w_dist == "normal" else wl.w_dist, seed=1)
-    t0 = time.perf_counter()
-    reference_gemm(xq, wq, xs, ws)
-    t128 = time.perf_counter() - t0
+    t128 = float("inf")
+    for _ in range(2):  # the first call is cold
+        t0 = time.perf_counter()
+        reference_gemm(xq, wq, xs, ws)
+        t128 = min(t128, time.perf_counter() - t0)
     per_step = args.ref_budget / max(1, args.steps + args.warmup)
     n_cols = int(min(wl.N, max(128, 128 * math.floor(per_step / max(t128, 1e-5)))))
     n_cols -= n_cols % 128
+    # below one 128-column weight block per step, sample fewer tokens too (the
+    # oracle's time is mostly the fp32 matmul, linear in the token count); the
+    # weight block's dequantisation (~2 ms at K = 7168 on 8 cores) is the
+    # floor of a step
+    m_rows = wl.M if per_step >= t128 else max(1, min(wl.M, int(wl.M * per_step / max(t128, 1e-9))))
+    xq, xs = xq[:m_rows], xs[:m_rows]
     wq, ws = data.make_weights(n_cols, wl.K, "normal" if wl.w_dist == "normal" else wl.w_dist, seed=1)
     for _ in range(args.warmup):
         reference_gemm(xq, wq, xs, ws)
@@ -567,8 +575,9 @@ def run_reference(args):
     for _ in range(args.steps):
         reference_gemm(xq, wq, xs, ws)
     dt = time.perf_counter() - t0
-    value = data.flops(wl.M, n_cols, wl.K) * args.steps / dt / 1e12
-    sample = (f"M={wl.M} x N={n_cols} (of {wl.N}) x K={wl.K} per step of workload {wl.name}: fp32 dequantise + "
+    value = data.flops(m_rows, n_cols, wl.K) * args.steps / dt / 1e12
+    sample = (f"M={m_rows} (of {wl.M}) x N={n_cols} (of {wl.N}) x K={wl.K} per step of workload {wl.name}: "
+              f"fp32 dequantise + "
               f"matmul + bf16 (client/aiter/hsa/gfx942/driver.py:18-20 restated), torch CPU, {threads} threads")
     line = {"metric": METRIC, "value": round(value, 5), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
