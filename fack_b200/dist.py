@@ -89,27 +89,47 @@ class CudaIpc:
         _lib.load().fack_ipc_close_handle(base)
 
 
+def _layout(t: torch.Tensor) -> tuple:
+    """(numel, element size, rows, row stride): what a peer's copy must match
+    for the same byte offsets to address the same elements."""
+    return (t.numel(), t.element_size(), t.shape[0] if t.dim() else 1, t.stride(0) if t.dim() else 1)
+
+
 def exchange_peer_addresses(t: torch.Tensor, ipc, group=None) -> list:
-    """Collective: every rank publishes (IPC handle, offset) of its tensor ``t``
-    and maps every other rank's.  Returns, for each rank j != this rank in rank
-    order, (mapped base, address of j's ``t``)."""
+    """Collective: every rank publishes (IPC handle, offset, layout) of its
+    tensor ``t`` and maps every other rank's.  Returns, for each rank j != this
+    rank in rank order, (mapped base, address of j's ``t``).
+
+    Every rank's ``t`` must have the same layout (element count, element size,
+    rows, row stride); otherwise every rank raises ``ValueError`` (they all see
+    the same records) and nothing stays mapped."""
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     h, off = ipc.handle(t)
     hb = ipc.HANDLE_BYTES
     if len(h) != hb:
         raise ValueError("IPC handle size mismatch")
-    rec = torch.tensor(list(h) + list(int(off).to_bytes(8, "little")), dtype=torch.uint8)
+    tail = [int(off)] + list(_layout(t))
+    rec = torch.tensor(list(h) + [b for v in tail for b in int(v).to_bytes(8, "little")], dtype=torch.uint8)
     if dist.get_backend(group) == "nccl":
         rec = rec.to(t.device)
     recs = [torch.empty_like(rec) for _ in range(world)]
     dist.all_gather(recs, rec, group=group)
+    raws = [bytes(r.cpu().tolist()) for r in recs]
+    fields = [[int.from_bytes(raw[hb + 8 * i:hb + 8 * i + 8], "little") for i in range(len(tail))] for raw in raws]
+    if any(f[1:] != fields[0][1:] for f in fields):
+        raise ValueError("ranks registered buffers of different layouts (numel, element size, rows, row stride): "
+                         + ", ".join(str(tuple(f[1:])) for f in fields))
     peers = []
-    for j, r in enumerate(recs):
-        if j == rank:
-            continue
-        raw = bytes(r.cpu().tolist())
-        base = ipc.open(raw[:hb])
-        peers.append((base, base + int.from_bytes(raw[hb:hb + 8], "little")))
+    try:
+        for j, raw in enumerate(raws):
+            if j == rank:
+                continue
+            base = ipc.open(raw[:hb])
+            peers.append((base, base + fields[j][0]))
+    except BaseException:
+        for base, _ in peers:       # release what was mapped before the failure
+            ipc.close(base)
+        raise
     return peers
 
 
@@ -139,7 +159,11 @@ class ShardedBlockscaleGemm:
         self.interleave = interleave or _default_interleave
         self.ipc = ipc
         self._gather = None
-        self._peers: dict = {}     # (data_ptr, numel) of a registered out -> peer addresses of the same buffer
+        # (data_ptr, numel) of a registered out -> (that out, peer addresses of
+        # the same buffer).  Holding the tensor keeps its memory from being
+        # reused by another tensor at the same address while the peers still
+        # store into it; close() lets go.
+        self._peers: dict = {}
         self._mapped: list = []    # mapped peer bases, released by close()
         self._flag = None
 
@@ -162,8 +186,8 @@ class ShardedBlockscaleGemm:
                 self.ipc = CudaIpc()
             pairs = exchange_peer_addresses(out, self.ipc, self.group)
             self._mapped += [base for base, _ in pairs]
-            self._peers[key] = [addr for _, addr in pairs]
-        return self._peers[key]
+            self._peers[key] = (out, [addr for _, addr in pairs])
+        return self._peers[key][1]
 
     def _barrier(self, device) -> None:
         if self._flag is None or self._flag.device != torch.device(device):
@@ -171,7 +195,8 @@ class ShardedBlockscaleGemm:
         dist.all_reduce(self._flag, group=self.group)
 
     def close(self) -> None:
-        """Release the peer mappings (before the process group is destroyed)."""
+        """Release the peer mappings and the registered outputs (before the
+        process group is destroyed)."""
         for base in self._mapped:
             self.ipc.close(base)
         self._mapped, self._peers = [], {}

@@ -173,3 +173,76 @@ def test_fused_mode_contract():
     from fack_b200.dist import ShardedBlockscaleGemm
     with pytest.raises(ValueError):
         ShardedBlockscaleGemm.__init__(object.__new__(ShardedBlockscaleGemm), mode="ring")
+
+
+class _FailingIpc(_FakeIpc):
+    """Opens the first peer's handle, then fails (a mapping that cannot be made)."""
+
+    def open(self, handle):
+        if self.opened:
+            raise RuntimeError("fack_ipc_open_handle: simulated failure")
+        return super().open(handle)
+
+
+def _registry_worker(rank, world, port, case, result_dir):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from fack_b200.dist import ShardedBlockscaleGemm
+        outcome = "ok"
+        if case == "layout":
+            # rank 1's Y has one row more: the byte offsets would address other elements
+            gemm = ShardedBlockscaleGemm(mode="fused", ipc=_FakeIpc(rank))
+            try:
+                gemm.register(torch.zeros((8 + rank, 256), dtype=torch.bfloat16))
+            except ValueError as e:
+                outcome = "ValueError" if "layout" in str(e) else repr(e)
+            assert gemm.ipc.opened == [] and gemm._mapped == []
+        elif case == "open_fails":
+            ipc = _FailingIpc(rank)
+            gemm = ShardedBlockscaleGemm(mode="fused", ipc=ipc)
+            try:
+                gemm.register(torch.zeros((8, 384), dtype=torch.bfloat16))
+            except RuntimeError:
+                outcome = "RuntimeError"
+            # the one mapping made before the failure was released, nothing is registered
+            assert len(ipc.opened) == 1 and ipc.closed == [(ipc.opened[0] + 1) << 40], (ipc.opened, ipc.closed)
+            assert gemm._mapped == [] and gemm._peers == {}
+        (Path(result_dir) / f"{case}_{rank}").write_text(outcome)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case,world,want", [("layout", 2, "ValueError"), ("open_fails", 3, "RuntimeError")])
+def test_fused_registration_failures_leave_nothing_mapped(tmp_path, case, world, want):
+    mp.start_processes(_registry_worker, args=(world, _free_port(), case, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        assert (tmp_path / f"{case}_{r}").read_text() == want, f"rank {r}"
+
+
+def _holder_worker(rank, world, port):
+    import gc
+    import weakref
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from fack_b200.dist import ShardedBlockscaleGemm
+        gemm = ShardedBlockscaleGemm(mode="fused", ipc=_FakeIpc(rank))
+        out = torch.zeros((4, 256), dtype=torch.bfloat16)
+        ref = weakref.ref(out)
+        gemm.register(out)
+        del out
+        gc.collect()
+        assert ref() is not None      # registered: its memory cannot go to another tensor at the same address
+        gemm.close()
+        gc.collect()
+        assert ref() is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_registered_output_is_held_until_close():
+    mp.start_processes(_holder_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
