@@ -63,6 +63,9 @@ AITER_SYMBOLS = frozenset(
 KERNEL_PREFIX = "fack_bs_sm100"
 
 _workspaces: dict = {}
+# workspaces outgrown by a larger plan stay allocated: a CUDA graph captured
+# with one of them still launches into it on replay
+_retired_workspaces: list = []
 
 
 def _stream_handle(device: torch.device) -> int:
@@ -108,7 +111,7 @@ def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
 
 
 def workspace_size(M: int, N: int, K: int, split_k: int = 0, tile_m: int = 0, tile_n: int = 0) -> int:
-    """Bytes of split-K workspace for the plan (only needed with workspace="global")."""
+    """Bytes of split-K workspace for the plan (only used with reduce="global")."""
     return plan(M, N, K, tile_m, tile_n, split_k)[3]
 
 
@@ -122,6 +125,8 @@ def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
             raise RuntimeError(
                 "split-K workspace must grow during CUDA-graph capture; call the operator once "
                 "with this shape before capturing")
+        if ws is not None:
+            _retired_workspaces.append(ws)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws

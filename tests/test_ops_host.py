@@ -80,3 +80,19 @@ def test_ck_sibling_contract():
             fb.gemm_a8w8_blockscale_bpreshuffle_ck(a, b, xs, ws, out, kernelName=bad)
     with pytest.raises(ValueError, match="shuffle_weight"):
         fb.gemm_a8w8_blockscale_bpreshuffle_ck(a, b, xs, ws, out)
+
+
+def test_outgrown_workspace_stays_allocated(monkeypatch):
+    """A graph captured with the smaller workspace still launches into it on
+    replay, so growing the per-(device, stream) workspace keeps the old one."""
+    monkeypatch.setattr(ops, "_stream_handle", lambda device: 12345)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    monkeypatch.setattr(ops, "_workspaces", {})
+    monkeypatch.setattr(ops, "_retired_workspaces", [])
+    dev = torch.device("cpu")
+    small = ops._workspace(dev, 256)
+    assert ops._workspace(dev, 128) is small               # fits: reused
+    big = ops._workspace(dev, 4096)
+    assert big is not small and big.numel() == 4096
+    assert any(w is small for w in ops._retired_workspaces)
+    assert ops._workspace(dev, 0) is None
