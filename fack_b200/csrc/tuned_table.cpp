@@ -14,7 +14,8 @@
 // columns do not matter.  Required: cu_num, M, N, K, kernelName (this
 // library's fack_bs_sm100_t{16|32|64|128|256}x{64|128|256}_s{S}).  Optional: splitK
 // (must equal the name's S) and errRatio (must be 0).  Rows naming another
-// library's kernel (a gfx942 symbol) are skipped and counted.  The file is
+// library's kernel (a gfx942 symbol) are skipped and counted; a name with this
+// library's prefix that is not in the canonical form is an error.  The file is
 // checked whole before any row is added: a bad row leaves the table as it was.
 
 #include <stdio.h>
@@ -89,11 +90,16 @@ int bad_row(const char* path, int line, const char* why) {
 
 }  // namespace
 
-// fack_bs_sm100_t<tile_m>x<tile_n>_s<split>, nothing before or after.
+// fack_bs_sm100_t<tile_m>x<tile_n>_s<split>, nothing before or after, in the
+// canonical spelling only (no sign, space or leading zero), as the Python
+// layer's parser accepts it.
 bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp) {
   int n = -1;
   if (sscanf(name.c_str(), "fack_bs_sm100_t%dx%d_s%d%n", tm, bn, sp, &n) != 3) return false;
-  return n == static_cast<int>(name.size());
+  if (n != static_cast<int>(name.size())) return false;
+  char canon[64];
+  snprintf(canon, sizeof(canon), "fack_bs_sm100_t%dx%d_s%d", *tm, *bn, *sp);
+  return name == canon;
 }
 
 int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
@@ -188,6 +194,8 @@ int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skippe
       return bad_row(path, lineno, "cu_num, M, N, K must be integers");
     int tm, bn, sp;
     if (!parse_kernel_name(f[c_name], &tm, &bn, &sp)) {
+      if (f[c_name].rfind("fack_bs_sm100_", 0) == 0)
+        return bad_row(path, lineno, "malformed fack_bs_sm100 kernelName");
       ++skipped;  // another library's kernel
       continue;
     }

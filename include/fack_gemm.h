@@ -151,9 +151,11 @@ int fack_ipc_close_handle(void* base);
  * fack_gemm_bs_tuned_count / _clear: number of rows / remove all rows.
  * fack_gemm_bs_tuned_load: merge a CSV file.  '#' lines are comments, the
  *   first other line is a header, columns are found by name: cu_num, M, N, K,
- *   kernelName (fack_bs_sm100_t{128|256}x{64|128|256}_s{S}) are required,
- *   splitK (= S) and errRatio (= 0) are checked when present.  Rows naming
- *   another library's kernel are skipped and counted in *rows_skipped.  The
+ *   kernelName (fack_bs_sm100_t{128|256}x{64|128|256}_s{S}, or the swapped
+ *   small-M fack_bs_sm100_t{16|32|64}x128_s{S}) are required, splitK (= S)
+ *   and errRatio (= 0) are checked when present.  Rows naming another
+ *   library's kernel are skipped and counted in *rows_skipped; a name with
+ *   this library's prefix that is not in that canonical form is a bad row.  The
  *   whole file is checked before any row is added; on a bad row the table is
  *   unchanged, BAD_ARG is returned and fack_last_error gives "path:line: why".
  *   A later row for the same key replaces an earlier one.

@@ -95,6 +95,8 @@ GOOD = "148,1,3072,7168,fack_bs_sm100_t128x64_s1"
     (["cu_num,M,N,K,kernelName", GOOD, "148,256,3072,7168"], "field count"),
     (["cu_num,M,N,K,kernelName", GOOD, "148,256,3072,7168.5,fack_bs_sm100_t128x256_s5"], "integers"),
     (["cu_num,M,N,K,kernelName", GOOD, "148,256,384,7168,fack_bs_sm100_t128x256_s5"], "invalid for this shape"),
+    (["cu_num,M,N,K,kernelName", GOOD, "148,256,3072,7168,fack_bs_sm100_t0128x256_s5"], "malformed"),
+    (["cu_num,M,N,K,kernelName", GOOD, "148,256,3072,7168,fack_bs_sm100_t128x256_s+5"], "malformed"),
 ])
 def test_bad_file_leaves_table_unchanged(lib, tmp_path, rows, why):
     assert lib.fack_gemm_bs_tuned_set(148, 1, 128, 128, 128, 64, 1) == 0
