@@ -35,7 +35,7 @@ def test_every_declared_symbol_is_exported_and_typed():
 def test_status_strings_and_version():
     lib = _lib.load()
     assert lib.fack_version() == 100
-    for code in range(10):
+    for code in range(_lib.FACK_ERR_SCRATCH_LIMIT + 1):
         s = lib.fack_status_string(code).decode()
         assert s and s != "unknown status"
     assert lib.fack_status_string(99).decode() == "unknown status"
