@@ -52,6 +52,22 @@ WORKLOADS = {
 for _m in SWEEP_M:
     WORKLOADS[f"sweep_m{_m}"] = Workload(f"sweep_m{_m}", _m, 3072, 7168)
 
+# Workloads whose output columns are sharded over the GPUs of one node
+# (rank r computes Y[:, r*N/g : (r+1)*N/g]); the others run as replicas.
+SHARDED = ("prefill", "wide_constant", "wide_uniform")
+SHARD_COUNTS = (2, 4, 8)
+
+
+def shard_shapes() -> list:
+    """(M, N/g, K) of one rank's GEMM for every sharded workload and g in SHARD_COUNTS."""
+    out = []
+    for name in SHARDED:
+        wl = WORKLOADS[name]
+        for g in SHARD_COUNTS:
+            if wl.N % (BLOCK * g) == 0 and (wl.M, wl.N // g, wl.K) not in out:
+                out.append((wl.M, wl.N // g, wl.K))
+    return out
+
 
 def _safe_scale(amax: torch.Tensor) -> torch.Tensor:
     s = amax / QMAX

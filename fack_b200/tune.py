@@ -64,10 +64,12 @@ RECORD_SHAPES = (
 
 def default_shapes() -> list:
     """The reference's tuned workloads plus the benchmark workloads of this
-    library (decode M sweep, plumbing, prefill, wide layer)."""
+    library (decode M sweep, plumbing, prefill, wide layer) and one rank's
+    column shard of the sharded ones at 2, 4 and 8 GPUs."""
     shapes = list(RECORD_SHAPES)
     for wl in data.WORKLOADS.values():
         shapes.append((wl.M, wl.N, wl.K))
+    shapes += data.shard_shapes()
     out, seen = [], set()
     for s in shapes:
         if s not in seen:

@@ -149,6 +149,11 @@ def test_default_shapes_cover_the_reference_records_and_workloads():
     assert len(tune.RECORD_SHAPES) == 43 and len(set(tune.RECORD_SHAPES)) == 43
     assert set(tune.RECORD_SHAPES) <= set(shapes)
     assert (256, 3072, 7168) in shapes and (8192, 7168, 16384) in shapes and (32, 65536, 7168) in shapes
+    # one rank's shard of the column-sharded workloads at 2, 4 and 8 GPUs
+    for s in ((32, 32768, 7168), (32, 16384, 7168), (32, 8192, 7168),
+              (8192, 3584, 16384), (8192, 1792, 16384), (8192, 896, 16384)):
+        assert s in shapes, s
+    assert len(shapes) == len(set(shapes))
     assert all(n % 128 == 0 and k % 128 == 0 for _, n, k in shapes)
 
 
