@@ -96,3 +96,14 @@ def test_outgrown_workspace_stays_allocated(monkeypatch):
     assert big is not small and big.numel() == 4096
     assert any(w is small for w in ops._retired_workspaces)
     assert ops._workspace(dev, 0) is None
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    """No CPU or library fallback: without libfack_gemm.so every entry raises."""
+    from fack_b200 import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libfack_gemm.so")
+    with pytest.raises(RuntimeError, match="no fallback"):
+        _lib.load()
+    with pytest.raises(RuntimeError, match="no fallback"):
+        fb.get_config(256, 3072, 7168)
