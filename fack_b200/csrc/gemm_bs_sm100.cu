@@ -1092,8 +1092,7 @@ static int co_resident(DeviceInfo* d, int tm, int bn, int split) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, k.threads, k.smem) != cudaSuccess) return 0;
     n = per_sm * d->sms;
   } else {
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cx, 1, split);
     cfg.blockDim = dim3(k.threads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
@@ -1288,8 +1287,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   const KernelEntry& k = kernel_for(tm, bn);
   int gx, gy, gz;
   plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gx, gy, gz);
   cfg.blockDim = dim3(k.threads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;

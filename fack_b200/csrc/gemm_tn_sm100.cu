@@ -493,8 +493,7 @@ static int co_resident(DevState* d, int sms, int kind, int tm, int bn, int split
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k.fn, kThreads, k.smem) != cudaSuccess) return 0;
     n = per_sm * sms;
   } else {
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cx, 1, split);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
@@ -666,8 +665,7 @@ int fack_gemm_tn(int kind, const void* a, int64_t lda, const void* b, int b_pack
   p.timeout_ns = 2000000000ull;
 
   const Entry& k = kernel_for(kind, tm, bn);
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = plan_grid(M, N, tm, bn, sp);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;
