@@ -168,6 +168,22 @@ class ShapeBench:
         return statistics.median(times)
 
 
+def choose(results: list, heuristic_name: str, shape=None) -> tuple:
+    """The winning (us, kernelName, splitK, errRatio) of one shape's results:
+    the fastest plan with errRatio 0, unless the cost model's own plan passes
+    and is within KEEP_MARGIN of it (timing noise), which then stays.  Raises
+    RuntimeError if no plan passes the check."""
+    ok = [r for r in results if r[3] == 0.0]
+    if not ok:
+        raise RuntimeError(f"no plan of shape {shape} passed the output check: "
+                           + ", ".join(f"{r[1]} errRatio {r[3]}" for r in results))
+    best = min(ok)
+    heur_row = next((r for r in ok if r[1] == heuristic_name), None)
+    if heur_row and heur_row[0] <= best[0] * (1.0 + KEEP_MARGIN):
+        best = heur_row
+    return best
+
+
 def tune_shape(M: int, N: int, K: int, log=None) -> dict:
     """Time every plan of one shape; the fastest plan with errRatio 0 wins."""
     sb = ShapeBench(M, N, K)
@@ -180,11 +196,9 @@ def tune_shape(M: int, N: int, K: int, log=None) -> dict:
         results.append((us, name, sk, er))
         if log:
             log(f"  {name:28s} {us:9.2f} us  errRatio {er}")
-    best = min(r for r in results if r[3] == 0.0)
+    best = choose(results, heur["kernelName"], (M, N, K))
     heur_row = next((r for r in results if r[1] == heur["kernelName"]), None)
     heur_us = heur_row[0] if heur_row else float("nan")
-    if heur_row and heur_row[3] == 0.0 and heur_us <= best[0] * (1.0 + KEEP_MARGIN):
-        best = heur_row  # within timing noise of the best: keep the cost model's plan
     us = best[0]
     return {"cu_num": torch.cuda.get_device_properties(0).multi_processor_count, "M": M, "N": N, "K": K,
             "kernelName": best[1], "splitK": best[2], "us": round(us, 3),

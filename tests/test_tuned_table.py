@@ -172,3 +172,31 @@ def test_shipped_table_is_valid():
         assert float(r["us"]) <= float(r["heuristic_us"]) + 1e-6   # never slower than the cost model's plan
     lib = _lib.load()
     assert lib.fack_gemm_bs_tuned_count() >= len({(r["M"], r["N"], r["K"]) for r in rows})
+
+
+def test_tuner_choice_rule():
+    r = [(10.0, "fack_bs_sm100_t128x256_s5", 5, 0.0), (9.0, "fack_bs_sm100_t128x128_s6", 6, 0.0),
+         (5.0, "fack_bs_sm100_t128x64_s8", 8, 0.25)]                  # fastest, but fails the check
+    assert tune.choose(r, "fack_bs_sm100_t64x128_s1")[1] == "fack_bs_sm100_t128x128_s6"
+    # the cost model's plan within KEEP_MARGIN of the best stays
+    near = [(9.0 * (1 + tune.KEEP_MARGIN / 2), "fack_bs_sm100_t128x256_s5", 5, 0.0)] + r[1:]
+    assert tune.choose(near, "fack_bs_sm100_t128x256_s5")[1] == "fack_bs_sm100_t128x256_s5"
+    assert tune.choose(r, "fack_bs_sm100_t128x256_s5")[1] == "fack_bs_sm100_t128x128_s6"   # 11 % slower: replaced
+    assert tune.choose(r, "fack_bs_sm100_t128x64_s8")[1] == "fack_bs_sm100_t128x128_s6"    # failing plan never kept
+    with pytest.raises(RuntimeError, match="no plan"):
+        tune.choose([r[2]], "fack_bs_sm100_t128x64_s8", (256, 3072, 7168))
+
+
+def test_tuner_csv_loads_into_the_c_table(lib, tmp_path):
+    """write_csv's output is what fack_gemm_bs_tuned_load reads."""
+    rows = [{"cu_num": 148, "M": 256, "N": 3072, "K": 7168, "kernelName": "fack_bs_sm100_t128x256_s5",
+             "splitK": 5, "us": 14.5, "tflops": 777.0, "bw": 1758.0, "errRatio": 0,
+             "heuristic_kernelName": "fack_bs_sm100_t128x256_s5", "heuristic_us": 14.5, "bad_plans": []},
+            {"cu_num": 148, "M": 32, "N": 3072, "K": 7168, "kernelName": "fack_bs_sm100_t32x128_s5",
+             "splitK": 5, "us": 9.3, "tflops": 47.4, "bw": 2372.0, "errRatio": 0,
+             "heuristic_kernelName": "fack_bs_sm100_t128x256_s8", "heuristic_us": 10.4, "bad_plans": []}]
+    p = tmp_path / "tuned.csv"
+    tune.write_csv(rows, p)
+    assert _lib.load_tuned(p, lib) == (2, 0)
+    assert lookup(lib, 148, 256, 3072, 7168) == (128, 256, 5)
+    assert lookup(lib, 148, 32, 3072, 7168) == (32, 128, 5)
