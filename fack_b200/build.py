@@ -59,29 +59,32 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
-GEMM_LAUNCH_REGS = 168  # the kernel's setmaxnreg split is sized for this count
+GEMM_LAUNCH_REGS = 168  # the FP8 kernel's setmaxnreg split is sized for this count
+GEMM_SPLIT_VARIANTS = 6  # gemm_bs_kernel<64|128|256, single CTA|pair>
 
 
 def check_ptxas(log: str) -> None:
-    """Every GEMM kernel variant must use exactly GEMM_LAUNCH_REGS registers and
-    spill nothing (the host refuses to launch it otherwise)."""
+    """No kernel spills registers, and every variant of the register-split FP8
+    kernel (``gemm_bs_kernel``) uses exactly GEMM_LAUNCH_REGS registers, which
+    the host also checks before it launches one."""
     entry, found = None, 0
     for line in log.splitlines():
         m = re.search(r"Compiling entry function '(\S+)'", line)
         if m:
             entry = m.group(1)
             continue
-        if entry and "gemm_bs_kernel" in entry:
-            m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
-            if m and (int(m.group(1)) or int(m.group(2))):
-                raise RuntimeError(f"{entry} spills registers: {line.strip()}")
-            m = re.search(r"Used (\d+) registers", line)
-            if m:
-                found += 1
-                if int(m.group(1)) != GEMM_LAUNCH_REGS:
-                    raise RuntimeError(f"{entry} uses {m.group(1)} registers, expected {GEMM_LAUNCH_REGS}")
-    if found == 0:
-        raise RuntimeError("ptxas report lists no GEMM kernel")
+        if not entry:
+            continue
+        m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+        if m and (int(m.group(1)) or int(m.group(2))):
+            raise RuntimeError(f"{entry} spills registers: {line.strip()}")
+        m = re.search(r"Used (\d+) registers", line)
+        if m and "gemm_bs_kernel" in entry:
+            found += 1
+            if int(m.group(1)) != GEMM_LAUNCH_REGS:
+                raise RuntimeError(f"{entry} uses {m.group(1)} registers, expected {GEMM_LAUNCH_REGS}")
+    if found != GEMM_SPLIT_VARIANTS:
+        raise RuntimeError(f"ptxas report lists {found} gemm_bs_kernel variants, expected {GEMM_SPLIT_VARIANTS}")
 
 
 if __name__ == "__main__":
