@@ -1532,15 +1532,16 @@ typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
 
 int fack_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes, size_t* offset) {
   if (!ptr || !handle || !offset || handle_bytes < sizeof(cudaIpcMemHandle_t)) return FACK_ERR_BAD_ARG;
-  static AddressRangeFn range = nullptr;
-  if (!range) {
+  // looked up once; a function-local static is initialised thread-safely
+  static const AddressRangeFn range = []() -> AddressRangeFn {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      return fail(FACK_ERR_CUDA, "cuMemGetAddressRange entry point");
-    range = reinterpret_cast<AddressRangeFn>(fn);
-  }
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<AddressRangeFn>(fn);
+  }();
+  if (!range) return fail(FACK_ERR_CUDA, "cuMemGetAddressRange entry point");
   CUdeviceptr base = 0;
   size_t size = 0;
   if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)

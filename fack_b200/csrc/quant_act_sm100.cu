@@ -25,6 +25,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/fack_gemm.h"
 #include "fack_internal.h"
 #include "sm100_ptx.cuh"
@@ -165,6 +167,20 @@ __global__ void __launch_bounds__(kQThreads, 2) quant_act_kernel(const T* __rest
 
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Kernel attributes are set per device: one bit per (device, input type).
+constexpr int kMaxDevices = 64;
+static std::mutex g_configure_mu;
+static uint32_t g_configured[kMaxDevices];
+
+static bool configure_once(int dev, int bit, const void* fn, int smem) {
+  if (dev < 0 || dev >= kMaxDevices) return false;
+  std::lock_guard<std::mutex> lk(g_configure_mu);
+  if (g_configured[dev] & (1u << bit)) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
+  g_configured[dev] |= 1u << bit;
+  return true;
+}
+
 }  // namespace fack_quant
 
 extern "C" int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, int K, void* xq, int64_t ldq,
@@ -192,24 +208,14 @@ extern "C" int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, in
   const uint64_t tmo = 2000000000ull;  // 2 s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (x_dtype == FACK_DTYPE_F32) {
-    static bool configured = false;
-    if (!configured) {
-      if (cudaFuncSetAttribute(quant_act_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_f32) !=
-          cudaSuccess)
-        return FACK_ERR_LAUNCH;
-      configured = true;
-    }
+    if (!configure_once(dev, 0, reinterpret_cast<const void*>(quant_act_kernel<float>), smem_f32))
+      return FACK_ERR_LAUNCH;
     quant_act_kernel<float><<<blocks, kQThreads, smem_f32, s>>>(static_cast<const float*>(x), ldx, M, KB,
                                                                  static_cast<uint8_t*>(xq), ldq, x_scale, xs_stride_m,
                                                                  xs_stride_kb, status, tmo);
   } else {
-    static bool configured = false;
-    if (!configured) {
-      if (cudaFuncSetAttribute(quant_act_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem_bf16) != cudaSuccess)
-        return FACK_ERR_LAUNCH;
-      configured = true;
-    }
+    if (!configure_once(dev, 1, reinterpret_cast<const void*>(quant_act_kernel<__nv_bfloat16>), smem_bf16))
+      return FACK_ERR_LAUNCH;
     quant_act_kernel<__nv_bfloat16><<<blocks, kQThreads, smem_bf16, s>>>(
         static_cast<const __nv_bfloat16*>(x), ldx, M, KB, static_cast<uint8_t*>(xq), ldq, x_scale, xs_stride_m,
         xs_stride_kb, status, tmo);
