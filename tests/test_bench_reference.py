@@ -46,3 +46,16 @@ def test_reference_arm_line_and_budget(workload):
     # calibration call, so allow slack), plus interpreter start-up and data set-up
     assert line["ms_per_step"] * (steps + 3) / 1e3 < 4 * budget, line
     assert wall < 4 * budget + 60, wall
+
+
+@pytest.mark.parametrize("args,env_world,why", [
+    (["--warmup", "2"], "1", "--warmup must be >= 3"),
+    (["--gpus", "2"], "1", "launch N>1 with torchrun"),
+    (["--workload", "no_such_workload"], "1", "unknown workload"),
+])
+def test_contract_violations_refused(args, env_world, why):
+    env = dict(os.environ, WORLD_SIZE=env_world, RANK="0", LOCAL_RANK="0")
+    p = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", *args],
+                       capture_output=True, text=True, timeout=120, env=env, cwd=ROOT)
+    assert p.returncode == 2 and why in p.stderr, p.stderr[-500:]
+    assert p.stdout.strip() == ""
