@@ -50,6 +50,7 @@ SIGNATURES = {
     "fack_last_error": (ctypes.c_char_p, []),
     "fack_gemm_bs_select": (_c_int, [_c_int, _c_int, _c_int, _c_int,
                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "fack_gemm_bs_plan_estimate": (_c_int, [_c_int] * 6 + [ctypes.POINTER(ctypes.c_double)]),
     "fack_gemm_bs_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_sz)]),
     "fack_gemm_bs_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int),
                                    ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_sz)]),

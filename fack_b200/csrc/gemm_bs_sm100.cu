@@ -1407,6 +1407,17 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
   return FACK_OK;
 }
 
+int fack_gemm_bs_plan_estimate(int M, int N, int K, int tile_m, int tile_n, int split_k, double* cycles) {
+  if (!cycles) return FACK_ERR_BAD_ARG;
+  const int v = tuned_validate(M, N, K, tile_m, tile_n, split_k);  // the rules of an explicit plan
+  if (v != FACK_OK) return v;
+  DeviceInfo* d = nullptr;
+  const int st = device_info(&d);
+  if (st != FACK_OK) return st;
+  *cycles = plan_cost(d, M, N, K, tile_m, tile_n, split_k);
+  return FACK_OK;
+}
+
 int fack_gemm_bs_select(int M, int N, int K, int split_k_request, int* tile_n, int* split_k) {
   int tm = 0;
   return fack_gemm_bs_plan(M, N, K, 0, 0, split_k_request, &tm, tile_n, split_k, nullptr);

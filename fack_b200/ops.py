@@ -104,6 +104,16 @@ def plan(M: int, N: int, K: int, tile_m: int = 0, tile_n: int = 0, split_k: int 
     return tm.value, tn.value, sk.value, nb.value
 
 
+def plan_estimate(M: int, N: int, K: int, tile_m: int, tile_n: int, split_k: int) -> Optional[float]:
+    """The planner's cost-model estimate of an explicit plan in SM cycles on
+    the current device; None if the model would not offer the plan."""
+    lib = _lib.load()
+    cyc = ctypes.c_double()
+    _lib.check(lib.fack_gemm_bs_plan_estimate(int(M), int(N), int(K), int(tile_m), int(tile_n), int(split_k),
+                                              ctypes.byref(cyc)), "fack_gemm_bs_plan_estimate")
+    return None if cyc.value >= 1e29 else cyc.value
+
+
 def get_config(M: int, N: int, K: int, split_k: int = 0) -> dict:
     """Kernel and split-K this library uses for (M, N, K) on the current device."""
     tm, tn, sk, _ = plan(M, N, K, 0, 0, split_k)

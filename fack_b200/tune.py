@@ -1,6 +1,6 @@
 """Exact-shape plan tuner for the FP8 block-scaled GEMM.
 
-``python -m fack_b200.tune [--shapes M,N,K;M,N,K...] [--out CSV] [--verbose]``
+``python -m fack_b200.tune [--shapes M,N,K;M,N,K...] [--out CSV] [--log JSONL] [--verbose]``
 
 For every (M, N, K) the tuner times each valid plan of the kernel --
 token tile 128 (one CTA) or 256 (a CTA pair), weight tile 64, 128 or 256
@@ -18,7 +18,10 @@ CSV carrying kernelName, splitK, us, tflops, bw and errRatio
 (client/aiter/dispatch.py:23-35; a row with a non-zero errRatio is refused,
 dispatch.py:135-137).  The rows written here carry the same columns plus
 ``heuristic_kernelName`` / ``heuristic_us``, the cost model's plan and its
-time, so the gain of every override is on record.
+time, so the gain of every override is on record.  ``--log`` also writes one
+JSON line per timed plan -- measured µs, errRatio and the cost model's
+estimate in SM cycles (``fack_gemm_bs_plan_estimate``) -- the data for
+calibrating the model's rates against the hardware.
 
 Timing: each plan is captured in a CUDA graph of ``launches`` calls rotating
 over input sets larger than 2.5 x the 126 MB L2 together, replayed once to
@@ -188,12 +191,13 @@ def tune_shape(M: int, N: int, K: int, log=None) -> dict:
     """Time every plan of one shape; the fastest plan with errRatio 0 wins."""
     sb = ShapeBench(M, N, K)
     heur = ops.get_config(M, N, K)
-    results = []
+    results, plans = [], []
     for tm, tn, sk in candidates(M, N, K):
         name = ops.kernel_name(tm, tn, sk)
         er = sb.check(name)
         us = sb.time_us(name) if er == 0.0 else float("inf")
         results.append((us, name, sk, er))
+        plans.append(plan_record(M, N, K, name, us, er, ops.plan_estimate(M, N, K, tm, tn, sk)))
         if log:
             log(f"  {name:28s} {us:9.2f} us  errRatio {er}")
     best = choose(results, heur["kernelName"], (M, N, K))
@@ -205,7 +209,22 @@ def tune_shape(M: int, N: int, K: int, log=None) -> dict:
             "tflops": round(data.flops(M, N, K) / us / 1e6, 1),
             "bw": round(data.algorithmic_bytes(M, N, K) / us / 1e3, 1), "errRatio": 0,
             "heuristic_kernelName": heur["kernelName"], "heuristic_us": round(heur_us, 3),
-            "bad_plans": [r[1] for r in results if r[3] != 0.0]}
+            "bad_plans": [r[1] for r in results if r[3] != 0.0], "plans": plans}
+
+
+def plan_record(M: int, N: int, K: int, name: str, us: float, err: float, model_cycles) -> dict:
+    """One --log line: a timed plan with the cost model's estimate (None =
+    the model would not offer it; us None = failed the output check)."""
+    return {"M": M, "N": N, "K": K, "kernelName": name, "us": round(us, 3) if math.isfinite(us) else None,
+            "errRatio": err, "model_cycles": None if model_cycles is None else round(model_cycles, 1)}
+
+
+def write_log(rows: list, path: Path) -> None:
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with open(path, "w") as f:
+        for r in rows:
+            for rec in r.get("plans", []):
+                f.write(json.dumps(rec) + "\n")
 
 
 def write_csv(rows: list, path: Path) -> None:
@@ -231,6 +250,7 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--shapes", default="", help="M,N,K;M,N,K... (default: the tuned workloads)")
     ap.add_argument("--out", default=str(_lib.TUNED_TABLE))
+    ap.add_argument("--log", default="", help="write every timed plan with the cost model's estimate (JSONL)")
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
@@ -248,6 +268,8 @@ def main(argv=None) -> int:
                                               "heuristic_us", "bad_plans")}), flush=True)
         torch.cuda.empty_cache()
     write_csv(rows, Path(args.out))
+    if args.log:
+        write_log(rows, Path(args.log))
     bad = sum(len(r["bad_plans"]) for r in rows)
     print(json.dumps({"rows": len(rows), "out": args.out, "plans_failing_check": bad}))
     return 1 if bad else 0

@@ -109,6 +109,16 @@ int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
                         int* tile_n, int* split_k);
 
 /*
+ * The planner's cost-model estimate for one explicit plan (tile_m, tile_n,
+ * split_k all given, valid for the shape as for fack_gemm_bs_tuned_set), in
+ * SM cycles on the current device; 1e30 if the model would not offer it
+ * (e.g. swapped small-M tiles whose clusters are not all resident at once).
+ * For calibrating the model against measured times (python -m fack_b200.tune
+ * --log); it launches nothing.
+ */
+int fack_gemm_bs_plan_estimate(int M, int N, int K, int tile_m, int tile_n, int split_k, double* cycles);
+
+/*
  * fack_gemm_bs_ex that also stores every bf16 result to n_peers (0..7) more
  * copies of the output block, peer_outs[i] + (row * ldo + column), with the
  * same ldo: the fused compute + all-gather of the column-sharded multi-GPU

@@ -1,6 +1,7 @@
 """CPU: the exact-shape plan table (fack_gemm_bs_tuned_*), its CSV loader and
 the tuner's candidate set.  No device is touched: every call here is host-only."""
 import csv
+import json
 import ctypes
 import os
 import subprocess
@@ -200,3 +201,25 @@ def test_tuner_csv_loads_into_the_c_table(lib, tmp_path):
     assert _lib.load_tuned(p, lib) == (2, 0)
     assert lookup(lib, 148, 256, 3072, 7168) == (128, 256, 5)
     assert lookup(lib, 148, 32, 3072, 7168) == (32, 128, 5)
+
+
+def test_plan_estimate_validates_before_any_device_query(lib):
+    cyc = ctypes.c_double(-1.0)
+    assert lib.fack_gemm_bs_plan_estimate(0, 3072, 7168, 128, 256, 5, ctypes.byref(cyc)) == _lib.FACK_ERR_BAD_SHAPE
+    assert lib.fack_gemm_bs_plan_estimate(256, 3072, 7168, 0, 256, 5, ctypes.byref(cyc)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs_plan_estimate(256, 3072, 7168, 128, 96, 5, ctypes.byref(cyc)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs_plan_estimate(65, 3072, 7168, 64, 128, 5, ctypes.byref(cyc)) == _lib.FACK_ERR_BAD_ARG
+    assert lib.fack_gemm_bs_plan_estimate(256, 3072, 7168, 128, 256, 5, None) == _lib.FACK_ERR_BAD_ARG
+    assert cyc.value == -1.0
+
+
+def test_tuner_log_lines(tmp_path):
+    rec = tune.plan_record(256, 3072, 7168, "fack_bs_sm100_t128x256_s5", 14.4861, 0.0, 27311.26)
+    bad = tune.plan_record(256, 3072, 7168, "fack_bs_sm100_t128x64_s8", float("inf"), 0.25, None)
+    p = tmp_path / "plans.jsonl"
+    tune.write_log([{"plans": [rec, bad]}, {"plans": []}], p)
+    lines = [json.loads(ln) for ln in p.read_text().splitlines()]
+    assert lines == [{"M": 256, "N": 3072, "K": 7168, "kernelName": "fack_bs_sm100_t128x256_s5", "us": 14.486,
+                      "errRatio": 0.0, "model_cycles": 27311.3},
+                     {"M": 256, "N": 3072, "K": 7168, "kernelName": "fack_bs_sm100_t128x64_s8", "us": None,
+                      "errRatio": 0.25, "model_cycles": None}]
