@@ -219,6 +219,31 @@ def plan_record(M: int, N: int, K: int, name: str, us: float, err: float, model_
             "errRatio": err, "model_cycles": None if model_cycles is None else round(model_cycles, 1)}
 
 
+def model_report(records: list, margin: float = KEEP_MARGIN) -> dict:
+    """How well the cost model ranks plans, from --log records: per shape the
+    model's pick (lowest estimate among plans it offers and that passed), the
+    measured best, and the regret = pick's time / best time - 1.  Shapes whose
+    regret exceeds ``margin`` are listed worst first."""
+    shapes: dict = {}
+    for r in records:
+        if r["us"] is None:
+            continue
+        shapes.setdefault((r["M"], r["N"], r["K"]), []).append(r)
+    per = []
+    for key, rs in sorted(shapes.items()):
+        best = min(rs, key=lambda r: r["us"])
+        offered = [r for r in rs if r["model_cycles"] is not None]
+        if not offered:
+            continue
+        pick = min(offered, key=lambda r: r["model_cycles"])
+        per.append({"shape": "x".join(map(str, key)), "model_pick": pick["kernelName"], "pick_us": pick["us"],
+                    "best": best["kernelName"], "best_us": best["us"], "regret": pick["us"] / best["us"] - 1.0})
+    misses = sorted((p for p in per if p["regret"] > margin), key=lambda p: -p["regret"])
+    regrets = [p["regret"] for p in per]
+    return {"shapes": len(per), "mean_regret": sum(regrets) / len(regrets) if regrets else 0.0,
+            "max_regret": max(regrets, default=0.0), "misses": misses, "per_shape": per}
+
+
 def write_log(rows: list, path: Path) -> None:
     path.parent.mkdir(parents=True, exist_ok=True)
     with open(path, "w") as f:
@@ -251,8 +276,14 @@ def main(argv=None) -> int:
     ap.add_argument("--shapes", default="", help="M,N,K;M,N,K... (default: the tuned workloads)")
     ap.add_argument("--out", default=str(_lib.TUNED_TABLE))
     ap.add_argument("--log", default="", help="write every timed plan with the cost model's estimate (JSONL)")
+    ap.add_argument("--report", default="", help="summarise a --log file (the model's regret per shape; no GPU)")
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args(argv)
+    if args.report:
+        records = [json.loads(ln) for ln in Path(args.report).read_text().splitlines() if ln.strip()]
+        rep = model_report(records)
+        print(json.dumps({k: rep[k] for k in ("shapes", "mean_regret", "max_regret", "misses")}, indent=1))
+        return 0
     if not torch.cuda.is_available():
         print("tune: needs a CUDA device", file=sys.stderr)
         return 2

@@ -223,3 +223,22 @@ def test_tuner_log_lines(tmp_path):
                       "errRatio": 0.0, "model_cycles": 27311.3},
                      {"M": 256, "N": 3072, "K": 7168, "kernelName": "fack_bs_sm100_t128x64_s8", "us": None,
                       "errRatio": 0.25, "model_cycles": None}]
+
+
+def test_model_report_regret(tmp_path):
+    rec = tune.plan_record
+    log = [rec(256, 3072, 7168, "fack_bs_sm100_t128x256_s5", 14.5, 0.0, 26000.0),     # model's pick, 10 % slow
+           rec(256, 3072, 7168, "fack_bs_sm100_t128x128_s6", 13.18, 0.0, 27000.0),    # measured best
+           rec(256, 3072, 7168, "fack_bs_sm100_t128x64_s8", float("inf"), 0.5, 1.0),  # failed: ignored
+           rec(32, 3072, 7168, "fack_bs_sm100_t32x128_s5", 9.3, 0.0, 17000.0),        # pick = best
+           rec(32, 3072, 7168, "fack_bs_sm100_t32x128_s1", 8.0, 0.0, None)]           # not offered
+    rep = tune.model_report(log)
+    assert rep["shapes"] == 2
+    by = {p["shape"]: p for p in rep["per_shape"]}
+    assert by["256x3072x7168"]["regret"] == pytest.approx(14.5 / 13.18 - 1)
+    assert by["32x3072x7168"]["model_pick"] == "fack_bs_sm100_t32x128_s5"
+    assert by["32x3072x7168"]["regret"] == pytest.approx(9.3 / 8.0 - 1)   # the unoffered plan was faster
+    assert [m["shape"] for m in rep["misses"]] == ["32x3072x7168", "256x3072x7168"]
+    p = tmp_path / "plans.jsonl"
+    tune.write_log([{"plans": log}], p)
+    assert tune.main(["--report", str(p)]) == 0
