@@ -19,6 +19,10 @@ LIB_PATH = _HERE / "libfack_gemm.so"
 # AITER_CONFIG_GEMM_A8W8_BLOCKSCALE_BPRESHUFFLE (client/aiter/dispatch.py:29-30).
 TUNED_TABLE = _HERE / "configs" / "a8w8_blockscale_bpreshuffle_tuned_gemm.csv"
 TUNED_ENV = "FACK_CONFIG_GEMM_A8W8_BLOCKSCALE_BPRESHUFFLE"
+# The sibling families' (BF16 TN, INT8 per token) table, same form; the
+# shipped file is optional, more tables come from this variable.
+TN_TUNED_TABLE = _HERE / "configs" / "gemm_tn_tuned_gemm.csv"
+TN_TUNED_ENV = "FACK_CONFIG_GEMM_TN"
 
 # Status codes, mirrored from enum fack_status.
 FACK_OK = 0
@@ -78,6 +82,11 @@ SIGNATURES = {
     "fack_gemm_bs_tuned_count": (_c_int, []),
     "fack_gemm_bs_tuned_clear": (_c_int, []),
     "fack_gemm_bs_tuned_load": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "fack_gemm_tn_tuned_set": (_c_int, [_c_int] * 8),
+    "fack_gemm_tn_tuned_lookup": (_c_int, [_c_int] * 5 + [ctypes.POINTER(_c_int)] * 3),
+    "fack_gemm_tn_tuned_count": (_c_int, []),
+    "fack_gemm_tn_tuned_clear": (_c_int, []),
+    "fack_gemm_tn_tuned_load": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
 }
 
 _lib = None
@@ -104,24 +113,29 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
         _lib = lib
         for table in tuned_tables():
             load_tuned(table, lib)
+        for table in tuned_tables(sibling=True):
+            load_tuned(table, lib, sibling=True)
     return lib
 
 
-def tuned_tables() -> list:
-    """The plan tables loaded with the library, in merge order."""
-    tables = [TUNED_TABLE] if TUNED_TABLE.exists() else []
-    extra = os.environ.get(TUNED_ENV, "")
+def tuned_tables(sibling: bool = False) -> list:
+    """The plan tables loaded with the library, in merge order (the FP8
+    table's, or with ``sibling`` the BF16 / INT8 families')."""
+    shipped, env = (TN_TUNED_TABLE, TN_TUNED_ENV) if sibling else (TUNED_TABLE, TUNED_ENV)
+    tables = [shipped] if shipped.exists() else []
+    extra = os.environ.get(env, "")
     return tables + [Path(p) for p in extra.split(os.pathsep) if p]
 
 
-def load_tuned(path: os.PathLike | str, lib: ctypes.CDLL | None = None) -> tuple:
-    """Merge a tuned-plan CSV into the library's table; returns (rows loaded,
-    rows skipped because they name another library's kernel).  Raises
-    ValueError naming the file and line of the first bad row (the table is
-    then unchanged)."""
+def load_tuned(path: os.PathLike | str, lib: ctypes.CDLL | None = None, sibling: bool = False) -> tuple:
+    """Merge a tuned-plan CSV into the library's FP8 table (or with
+    ``sibling`` the BF16 / INT8 table); returns (rows loaded, rows skipped
+    because they name another kernel family).  Raises ValueError naming the
+    file and line of the first bad row (the table is then unchanged)."""
     lib = lib or load()
     n, skipped = ctypes.c_int(), ctypes.c_int()
-    st = lib.fack_gemm_bs_tuned_load(os.fsencode(str(path)), ctypes.byref(n), ctypes.byref(skipped))
+    fn = lib.fack_gemm_tn_tuned_load if sibling else lib.fack_gemm_bs_tuned_load
+    st = fn(os.fsencode(str(path)), ctypes.byref(n), ctypes.byref(skipped))
     if st != FACK_OK:
         raise ValueError(f"tuned table {path}: {lib.fack_status_string(st).decode()}: "
                          f"{lib.fack_last_error().decode()}")

@@ -46,6 +46,7 @@
 #include "../../include/fack_gemm.h"
 #include "fack_internal.h"
 #include "sm100_ptx.cuh"
+#include "tuned_table.h"
 
 namespace fack_tn {
 
@@ -582,6 +583,10 @@ int fack_gemm_tn_plan(int kind, int M, int N, int K, int tile_m_request, int til
   int sms = 0;
   st = dev_state(&d, &sms);
   if (st != FACK_OK) return st;
+  // an exact-shape row of the sibling table fixes a fully automatic plan
+  if (!tile_m_request && !tile_n_request && !split_k_request &&
+      fack::tn_tuned_lookup(kind, sms, M, N, K, tile_m, tile_n, split_k))
+    return FACK_OK;
   double best = 1e30;
   int bt = 0, bb = 0, bs = 0;
   for (int tm : {128, 256}) {

@@ -1,22 +1,26 @@
-// tuned_table.cpp -- exact-shape (tile, split-K) overrides for the FP8
-// block-scaled GEMM planner.
+// tuned_table.cpp -- exact-shape (tile, split-K) overrides for the GEMM
+// planners: the FP8 block-scaled GEMM (fack_gemm_bs_plan) and the sibling
+// BF16 / INT8 families (fack_gemm_tn_plan).
 //
 // The reference picks its kernel by an exact (cu_num, M, N, K) row of a tuned
 // CSV (client/aiter/dispatch.py:23-35 names the blockscale-preshuffle table
 // and its key columns "M N K"; rows carry kernelName and splitK, and a row
 // reporting a non-zero error ratio is refused, dispatch.py:135-137).  This
-// file holds the B200 counterpart: a table keyed by (SM count, M, N, K) whose
-// rows fix the token tile, weight tile and split-K of fack_gemm_bs_plan's
-// automatic choice.  Shapes without a row keep the cost-model plan.
+// file holds the B200 counterpart: one table keyed by (family, SM count, M, N,
+// K) whose rows fix the token tile, weight tile and split-K of a planner's
+// fully automatic choice.  Shapes without a row keep the cost-model plan.
 //
-// CSV form read by fack_gemm_bs_tuned_load: '#' lines are comments; the first
-// other line is a header; columns are found by name, so order and extra
-// columns do not matter.  Required: cu_num, M, N, K, kernelName (this
-// library's fack_bs_sm100_t{16|32|64|128|256}x{64|128|256}_s{S}).  Optional: splitK
-// (must equal the name's S) and errRatio (must be 0).  Rows naming another
-// library's kernel (a gfx942 symbol) are skipped and counted; a name with this
-// library's prefix that is not in the canonical form is an error.  The file is
-// checked whole before any row is added: a bad row leaves the table as it was.
+// CSV form read by fack_gemm_bs_tuned_load / fack_gemm_tn_tuned_load: '#'
+// lines are comments; the first other line is a header; columns are found by
+// name, so order and extra columns do not matter.  Required: cu_num, M, N, K,
+// kernelName -- for the FP8 table this library's
+// fack_bs_sm100_t{16|32|64|128|256}x{64|128|256}_s{S}, for the sibling table
+// fack_tn_sm100_{bf16|i8}_t{128|256}x{64|128|256}_s{S} (the name gives the
+// family).  Optional: splitK (must equal the name's S) and errRatio (must be
+// 0).  Rows naming another kernel family (a gfx942 symbol, or the other table's
+// names) are skipped and counted; a name with the table's own prefix that is
+// not in the canonical form is an error.  The file is checked whole before any
+// row is added: a bad row leaves the table as it was.
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -35,7 +39,11 @@
 namespace fack {
 namespace {
 
-using Key = std::tuple<int, int, int, int>;  // cu_num, M, N, K
+// Family of a row: the FP8 block-scaled GEMM, or a sibling kind
+// (FACK_GEMM_BF16 / FACK_GEMM_I8).
+constexpr int kFamilyBlockscale = 100;
+
+using Key = std::tuple<int, int, int, int, int>;  // family, cu_num, M, N, K
 
 struct Plan {
   int tile_m, tile_n, split_k;
@@ -88,78 +96,50 @@ int bad_row(const char* path, int line, const char* why) {
   return record_error(FACK_ERR_BAD_ARG, msg);
 }
 
-}  // namespace
-
-// fack_bs_sm100_t<tile_m>x<tile_n>_s<split>, nothing before or after, in the
-// canonical spelling only (no sign, space or leading zero), as the Python
-// layer's parser accepts it.
-bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp) {
+// fack_tn_sm100_<bf16|i8>_t<tile_m>x<tile_n>_s<split>, canonical spelling only.
+bool parse_tn_name(const std::string& name, int* kind, int* tm, int* bn, int* sp) {
+  char fam[8] = {0};
   int n = -1;
-  if (sscanf(name.c_str(), "fack_bs_sm100_t%dx%d_s%d%n", tm, bn, sp, &n) != 3) return false;
+  if (sscanf(name.c_str(), "fack_tn_sm100_%7[a-z0-9]_t%dx%d_s%d%n", fam, tm, bn, sp, &n) != 4) return false;
   if (n != static_cast<int>(name.size())) return false;
+  if (strcmp(fam, "bf16") == 0) {
+    *kind = FACK_GEMM_BF16;
+  } else if (strcmp(fam, "i8") == 0) {
+    *kind = FACK_GEMM_I8;
+  } else {
+    return false;
+  }
   char canon[64];
-  snprintf(canon, sizeof(canon), "fack_bs_sm100_t%dx%d_s%d", *tm, *bn, *sp);
+  snprintf(canon, sizeof(canon), "fack_tn_sm100_%s_t%dx%d_s%d", fam, *tm, *bn, *sp);
   return name == canon;
 }
 
-int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
-  if (M < 1 || N < 128 || K < 128 || N % 128 || K % 128 || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
-  if (tile_m == 16 || tile_m == 32 || tile_m == 64) {  // swapped small-M tiles: 128 weight rows, all M tokens
-    if (M > tile_m || tile_n != 128 || split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128 ||
-        (K / 128 + split_k - 1) / split_k > 128)
-      return FACK_ERR_BAD_ARG;
-    return FACK_OK;
-  }
-  if (tile_m != 128 && tile_m != 256) return FACK_ERR_BAD_ARG;
-  if ((tile_n != 64 && tile_n != 128 && tile_n != 256) || N % tile_n) return FACK_ERR_BAD_ARG;
-  if (split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128) return FACK_ERR_BAD_ARG;
-  if (tile_m == 256 && 2 * split_k > kTunedMaxSplit) return FACK_ERR_BAD_ARG;
-  return FACK_OK;
+// A fully specified sibling plan checked by the sibling planner's own rules
+// (with all three given it answers without a device query).
+int tn_validate(int kind, int M, int N, int K, int tm, int bn, int sp) {
+  if (tm == 0 || bn == 0 || sp == 0) return FACK_ERR_BAD_ARG;
+  int a, b, c;
+  return fack_gemm_tn_plan(kind, M, N, K, tm, bn, sp, &a, &b, &c);
 }
 
-bool tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  const auto it = g_rows.find(Key(cu_num, M, N, K));
-  if (it == g_rows.end()) return false;
-  *tile_m = it->second.tile_m;
-  *tile_n = it->second.tile_n;
-  *split_k = it->second.split_k;
-  return true;
+// Which kernel names a table reads, and how a row is checked.
+struct TableKind {
+  const char* prefix;  // names with this prefix belong to the table (malformed ones are errors)
+  bool (*parse)(const std::string& name, int* family, int* tm, int* bn, int* sp);
+  int (*validate)(int family, int M, int N, int K, int tm, int bn, int sp);
+};
+
+bool parse_bs_row_name(const std::string& name, int* family, int* tm, int* bn, int* sp) {
+  *family = kFamilyBlockscale;
+  return parse_kernel_name(name, tm, bn, sp);
 }
 
-}  // namespace fack
+int validate_bs_row(int, int M, int N, int K, int tm, int bn, int sp) { return tuned_validate(M, N, K, tm, bn, sp); }
 
-using namespace fack;
+const TableKind kBlockscaleTable = {"fack_bs_sm100_", parse_bs_row_name, validate_bs_row};
+const TableKind kSiblingTable = {"fack_tn_sm100_", parse_tn_name, tn_validate};
 
-extern "C" {
-
-int fack_gemm_bs_tuned_set(int cu_num, int M, int N, int K, int tile_m, int tile_n, int split_k) {
-  if (cu_num < 1) return FACK_ERR_BAD_ARG;
-  const int st = tuned_validate(M, N, K, tile_m, tile_n, split_k);
-  if (st != FACK_OK) return st;
-  std::lock_guard<std::mutex> lk(g_mu);
-  g_rows[Key(cu_num, M, N, K)] = Plan{tile_m, tile_n, split_k};
-  return FACK_OK;
-}
-
-int fack_gemm_bs_tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
-  if (!tile_m || !tile_n || !split_k) return FACK_ERR_BAD_ARG;
-  if (!tuned_lookup(cu_num, M, N, K, tile_m, tile_n, split_k)) *tile_m = *tile_n = *split_k = 0;
-  return FACK_OK;
-}
-
-int fack_gemm_bs_tuned_count(void) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  return static_cast<int>(g_rows.size());
-}
-
-int fack_gemm_bs_tuned_clear(void) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  g_rows.clear();
-  return FACK_OK;
-}
-
-int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skipped) {
+int load_csv(const char* path, const TableKind& table, int* rows_loaded, int* rows_skipped) {
   if (!path) return FACK_ERR_BAD_ARG;
   std::ifstream in(path);
   if (!in) return record_error(FACK_ERR_BAD_ARG, "tuned table: cannot open file");
@@ -192,15 +172,18 @@ int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skippe
     int cu, M, N, K;
     if (!parse_int(f[c_cu], &cu) || !parse_int(f[c_m], &M) || !parse_int(f[c_n], &N) || !parse_int(f[c_k], &K))
       return bad_row(path, lineno, "cu_num, M, N, K must be integers");
-    int tm, bn, sp;
-    if (!parse_kernel_name(f[c_name], &tm, &bn, &sp)) {
-      if (f[c_name].rfind("fack_bs_sm100_", 0) == 0)
-        return bad_row(path, lineno, "malformed fack_bs_sm100 kernelName");
-      ++skipped;  // another library's kernel
+    int fam, tm, bn, sp;
+    if (!table.parse(f[c_name], &fam, &tm, &bn, &sp)) {
+      if (f[c_name].rfind(table.prefix, 0) == 0) {
+        char why[96];
+        snprintf(why, sizeof(why), "malformed %.20s kernelName", table.prefix);
+        return bad_row(path, lineno, why);
+      }
+      ++skipped;  // another kernel family's row
       continue;
     }
     if (cu < 1) return bad_row(path, lineno, "cu_num must be >= 1");
-    if (tuned_validate(M, N, K, tm, bn, sp) != FACK_OK)
+    if (table.validate(fam, M, N, K, tm, bn, sp) != FACK_OK)
       return bad_row(path, lineno, "kernelName's tile or split is invalid for this shape");
     if (c_split >= 0) {
       int s2;
@@ -210,7 +193,7 @@ int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skippe
       double e;
       if (!parse_double(f[c_err], &e) || e != 0.0) return bad_row(path, lineno, "row reports a non-zero errRatio");
     }
-    rows.emplace_back(Key(cu, M, N, K), Plan{tm, bn, sp});
+    rows.emplace_back(Key(fam, cu, M, N, K), Plan{tm, bn, sp});
   }
   if (header.empty()) return record_error(FACK_ERR_BAD_ARG, "tuned table: no header line");
   {
@@ -220,6 +203,130 @@ int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skippe
   if (rows_loaded) *rows_loaded = static_cast<int>(rows.size());
   if (rows_skipped) *rows_skipped = skipped;
   return FACK_OK;
+}
+
+bool is_sibling(int family) { return family == FACK_GEMM_BF16 || family == FACK_GEMM_I8; }
+
+int count_rows(bool sibling) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int n = 0;
+  for (const auto& r : g_rows) n += is_sibling(std::get<0>(r.first)) == sibling;
+  return n;
+}
+
+void clear_rows(bool sibling) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (auto it = g_rows.begin(); it != g_rows.end();) {
+    if (is_sibling(std::get<0>(it->first)) == sibling)
+      it = g_rows.erase(it);
+    else
+      ++it;
+  }
+}
+
+bool lookup(int family, int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const auto it = g_rows.find(Key(family, cu_num, M, N, K));
+  if (it == g_rows.end()) return false;
+  *tile_m = it->second.tile_m;
+  *tile_n = it->second.tile_n;
+  *split_k = it->second.split_k;
+  return true;
+}
+
+}  // namespace
+
+// fack_bs_sm100_t<tile_m>x<tile_n>_s<split>, nothing before or after, in the
+// canonical spelling only (no sign, space or leading zero), as the Python
+// layer's parser accepts it.
+bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp) {
+  int n = -1;
+  if (sscanf(name.c_str(), "fack_bs_sm100_t%dx%d_s%d%n", tm, bn, sp, &n) != 3) return false;
+  if (n != static_cast<int>(name.size())) return false;
+  char canon[64];
+  snprintf(canon, sizeof(canon), "fack_bs_sm100_t%dx%d_s%d", *tm, *bn, *sp);
+  return name == canon;
+}
+
+int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
+  if (M < 1 || N < 128 || K < 128 || N % 128 || K % 128 || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
+  if (tile_m == 16 || tile_m == 32 || tile_m == 64) {  // swapped small-M tiles: 128 weight rows, all M tokens
+    if (M > tile_m || tile_n != 128 || split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128 ||
+        (K / 128 + split_k - 1) / split_k > 128)
+      return FACK_ERR_BAD_ARG;
+    return FACK_OK;
+  }
+  if (tile_m != 128 && tile_m != 256) return FACK_ERR_BAD_ARG;
+  if ((tile_n != 64 && tile_n != 128 && tile_n != 256) || N % tile_n) return FACK_ERR_BAD_ARG;
+  if (split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128) return FACK_ERR_BAD_ARG;
+  if (tile_m == 256 && 2 * split_k > kTunedMaxSplit) return FACK_ERR_BAD_ARG;
+  return FACK_OK;
+}
+
+bool tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
+  return lookup(kFamilyBlockscale, cu_num, M, N, K, tile_m, tile_n, split_k);
+}
+
+bool tn_tuned_lookup(int kind, int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
+  return is_sibling(kind) && lookup(kind, cu_num, M, N, K, tile_m, tile_n, split_k);
+}
+
+}  // namespace fack
+
+using namespace fack;
+
+extern "C" {
+
+int fack_gemm_bs_tuned_set(int cu_num, int M, int N, int K, int tile_m, int tile_n, int split_k) {
+  if (cu_num < 1) return FACK_ERR_BAD_ARG;
+  const int st = tuned_validate(M, N, K, tile_m, tile_n, split_k);
+  if (st != FACK_OK) return st;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_rows[Key(kFamilyBlockscale, cu_num, M, N, K)] = Plan{tile_m, tile_n, split_k};
+  return FACK_OK;
+}
+
+int fack_gemm_bs_tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
+  if (!tile_m || !tile_n || !split_k) return FACK_ERR_BAD_ARG;
+  if (!tuned_lookup(cu_num, M, N, K, tile_m, tile_n, split_k)) *tile_m = *tile_n = *split_k = 0;
+  return FACK_OK;
+}
+
+int fack_gemm_bs_tuned_count(void) { return count_rows(false); }
+
+int fack_gemm_bs_tuned_clear(void) {
+  clear_rows(false);
+  return FACK_OK;
+}
+
+int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skipped) {
+  return load_csv(path, kBlockscaleTable, rows_loaded, rows_skipped);
+}
+
+int fack_gemm_tn_tuned_set(int kind, int cu_num, int M, int N, int K, int tile_m, int tile_n, int split_k) {
+  if (!is_sibling(kind) || cu_num < 1) return FACK_ERR_BAD_ARG;
+  const int st = tn_validate(kind, M, N, K, tile_m, tile_n, split_k);
+  if (st != FACK_OK) return st;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_rows[Key(kind, cu_num, M, N, K)] = Plan{tile_m, tile_n, split_k};
+  return FACK_OK;
+}
+
+int fack_gemm_tn_tuned_lookup(int kind, int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k) {
+  if (!tile_m || !tile_n || !split_k || !is_sibling(kind)) return FACK_ERR_BAD_ARG;
+  if (!tn_tuned_lookup(kind, cu_num, M, N, K, tile_m, tile_n, split_k)) *tile_m = *tile_n = *split_k = 0;
+  return FACK_OK;
+}
+
+int fack_gemm_tn_tuned_count(void) { return count_rows(true); }
+
+int fack_gemm_tn_tuned_clear(void) {
+  clear_rows(true);
+  return FACK_OK;
+}
+
+int fack_gemm_tn_tuned_load(const char* path, int* rows_loaded, int* rows_skipped) {
+  return load_csv(path, kSiblingTable, rows_loaded, rows_skipped);
 }
 
 }  // extern "C"

@@ -1,6 +1,9 @@
-// tuned_table.h -- internal interface of the exact-shape plan table
-// (tuned_table.cpp) used by the GEMM planner (gemm_bs_sm100.cu).
+// tuned_table.h -- internal interface of the exact-shape plan tables
+// (tuned_table.cpp) used by the GEMM planners (gemm_bs_sm100.cu,
+// gemm_tn_sm100.cu).
 #pragma once
+
+#include <string>
 
 #include "fack_internal.h"
 
@@ -16,7 +19,14 @@ constexpr int kTunedMaxSplit = 8;  // the GEMM's cluster limit along K
 // FACK_* status.
 int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k);
 
-// The row for (cu_num, M, N, K), if any.  Thread-safe.
+// The FP8 table's row for (cu_num, M, N, K), if any.  Thread-safe.
 bool tuned_lookup(int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k);
+
+// The sibling table's row for (kind = FACK_GEMM_BF16 | FACK_GEMM_I8, cu_num,
+// M, N, K), if any.  Thread-safe.
+bool tn_tuned_lookup(int kind, int cu_num, int M, int N, int K, int* tile_m, int* tile_n, int* split_k);
+
+// fack_bs_sm100_t<tile_m>x<tile_n>_s<split> in its canonical spelling.
+bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp);
 
 }  // namespace fack

@@ -1,6 +1,7 @@
 """Exact-shape plan tuner for the FP8 block-scaled GEMM.
 
-``python -m fack_b200.tune [--shapes M,N,K;M,N,K...] [--out CSV] [--log JSONL] [--verbose]``
+``python -m fack_b200.tune [--family blockscale|bf16|i8|siblings] [--shapes M,N,K;M,N,K...] [--out CSV]
+[--log JSONL] [--verbose]``
 
 For every (M, N, K) the tuner times each valid plan of the kernel --
 token tile 128 (one CTA) or 256 (a CTA pair), weight tile 64, 128 or 256
@@ -22,6 +23,13 @@ time, so the gain of every override is on record.  ``--log`` also writes one
 JSON line per timed plan -- measured µs, errRatio and the cost model's
 estimate in SM cycles (``fack_gemm_bs_plan_estimate``) -- the data for
 calibrating the model's rates against the hardware.
+
+``--family bf16|i8|siblings`` tunes the sibling families instead
+(``fack_gemm_tn``: BF16 TN and INT8 per token) over the same kind of plan
+list -- token tile 128 or 256, weight tile 64/128/256, split-K -- into the
+sibling table (``configs/gemm_tn_tuned_gemm.csv``, read by
+``fack_gemm_tn_tuned_load``); INT8 plans must match the exact epilogue
+bitwise, BF16 plans an fp32 matmul within 1e-2.
 
 Timing: each plan is captured in a CUDA graph of ``launches`` calls rotating
 over input sets larger than 2.5 x the 126 MB L2 together, replayed once to
@@ -148,27 +156,34 @@ class ShapeBench:
         return err_ratio(self.out[self.rows], self.ref)
 
     def time_us(self, name: str, repeats: int = 3) -> float:
-        stream = torch.cuda.Stream()
-        with torch.cuda.stream(stream):
-            for i in range(len(self.sets)):  # first calls outside capture
-                self.call(i, name)
-        stream.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(self.launches):
-                self.call(i, name)
-        times = []
-        with torch.cuda.stream(stream):
+        return _graph_time(lambda i: self.call(i, name), len(self.sets), self.launches, repeats)
+
+
+def _graph_time(call, n_sets: int, launches: int, repeats: int = 3) -> float:
+    """Median µs per call of ``call(i)`` captured ``launches`` times in a CUDA
+    graph (i rotating over the input sets), replayed once to warm up, then
+    ``repeats`` timed replays (CUDA events on the launch stream)."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(n_sets):  # first calls outside capture
+            call(i)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(launches):
+            call(i % n_sets)
+    times = []
+    with torch.cuda.stream(stream):
+        g.replay()
+        for _ in range(repeats):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
             g.replay()
-            for _ in range(repeats):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                g.replay()
-                b.record(stream)
-                b.synchronize()
-                times.append(a.elapsed_time(b) * 1e3 / self.launches)
-        g.reset()
-        return statistics.median(times)
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b) * 1e3 / launches)
+    g.reset()
+    return statistics.median(times)
 
 
 def choose(results: list, heuristic_name: str, shape=None) -> tuple:
@@ -252,10 +267,121 @@ def write_log(rows: list, path: Path) -> None:
                 f.write(json.dumps(rec) + "\n")
 
 
-def write_csv(rows: list, path: Path) -> None:
+# ------------------------------------------- sibling families (fack_gemm_tn) --
+
+SIBLING_FAMILIES = ("bf16", "i8")
+
+
+def sibling_default_shapes() -> list:
+    """The decode layer's M sweep at N = 3072, K = 7168 and a large 8192^3 problem."""
+    return [(m, 3072, 7168) for m in data.SWEEP_M] + [(8192, 8192, 8192)]
+
+
+def sibling_candidates(family: str, M: int, N: int, K: int) -> list:
+    """Every (tile_m, tile_n, split_k) fack_gemm_tn_plan accepts for the shape:
+    tile_m 128 or 256 (a CTA pair), tile_n 64/128/256 dividing N, split-K up to
+    min(8, K chunks of 128 bytes), 4 for pairs."""
+    chunks = K * (2 if family == "bf16" else 1) // 128
+    plans = []
+    for tm in (128, 256):
+        for tn in (256, 128, 64):
+            if N % tn:
+                continue
+            for sk in range(1, min(8 if tm == 128 else 4, chunks) + 1):
+                plans.append((tm, tn, sk))
+    return plans
+
+
+class SiblingShapeBench:
+    """Input sets and the reference for one sibling shape: INT8 checked
+    bitwise against the exact epilogue ((float(acc) * sa) * sb, each an fp32
+    rounding), BF16 within 1e-2 of an fp32 matmul."""
+
+    def __init__(self, family: str, M: int, N: int, K: int, seed: int = 0, launches: int = 24):
+        from . import siblings
+        self.siblings = siblings
+        dev = torch.device("cuda")
+        self.family = family
+        es = 2 if family == "bf16" else 1
+        n_sets = max(1, math.ceil(2.5 * L2_BYTES / ((M + N) * K * es)))
+        self.sets = []
+        for i in range(n_sets):
+            g = torch.Generator(device=dev).manual_seed(seed + i)
+            if family == "bf16":
+                a = (torch.randn((M, K), generator=g, device=dev) * 0.25).bfloat16()
+                b = (torch.randn((N, K), generator=g, device=dev) * 0.25).bfloat16()
+                sa = sb = None
+            else:
+                a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+                b = torch.randint(-128, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+                sa = 0.001 + 0.01 * torch.rand(M, generator=g, device=dev)
+                sb = 0.001 + 0.01 * torch.rand(N, generator=g, device=dev)
+            self.sets.append((a, ops.shuffle_weight(b), b, sa, sb))
+        a, _, b, sa, sb = self.sets[0]
+        self.rows = torch.arange(M, device=dev) if M <= 1024 else torch.linspace(0, M - 1, 512, device=dev).long()
+        if family == "bf16":
+            prev = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = False
+            try:
+                self.ref = a[self.rows].float() @ b.float().T
+            finally:
+                torch.backends.cuda.matmul.allow_tf32 = prev
+        else:
+            acc = a[self.rows].double() @ b.double().T        # exact: |sum| <= 2^14 * K < 2^53
+            self.ref = ((acc.float() * sa[self.rows, None]) * sb[None, :]).bfloat16()
+        self.out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        self.launches = max(launches, len(self.sets))
+
+    def call(self, i: int, plan: tuple):
+        a, bp, _, sa, sb = self.sets[i % len(self.sets)]
+        tm, tn, sk = plan
+        self.siblings.gemm_tn(a, bp, self.out, a_scale=sa, b_scale=sb, tile_m=tm, tile_n=tn, split_k=sk)
+
+    def check(self, plan: tuple) -> float:
+        self.call(0, plan)
+        torch.cuda.synchronize()
+        y = self.out[self.rows]
+        if self.family == "i8":
+            return float((y.view(torch.int16) != self.ref.view(torch.int16)).float().mean())
+        return err_ratio(y, self.ref)
+
+    def time_us(self, plan: tuple, repeats: int = 3) -> float:
+        return _graph_time(lambda i: self.call(i, plan), len(self.sets), self.launches, repeats)
+
+
+def tune_sibling_shape(family: str, M: int, N: int, K: int, log=None) -> dict:
+    """Time every plan of one sibling shape; the fastest plan that passes wins
+    (the cost model's own plan stays when within KEEP_MARGIN of it)."""
+    from . import siblings
+    kind = siblings.KINDS[torch.bfloat16 if family == "bf16" else torch.int8]
+    sb = SiblingShapeBench(family, M, N, K)
+    heur = siblings.get_config(kind, M, N, K)
+    results, plans = [], []
+    for plan in sibling_candidates(family, M, N, K):
+        name = siblings.kernel_name(kind, *plan)
+        er = sb.check(plan)
+        us = sb.time_us(plan) if er == 0.0 else float("inf")
+        results.append((us, name, plan[2], er))
+        plans.append(plan_record(M, N, K, name, us, er, None))
+        if log:
+            log(f"  {name:32s} {us:9.2f} us  errRatio {er}")
+    best = choose(results, heur["kernelName"], (family, M, N, K))
+    heur_row = next((r for r in results if r[1] == heur["kernelName"]), None)
+    es = 2 if family == "bf16" else 1
+    algo = (M * K + N * K) * es + 2 * M * N + (4 * (M + N) if family == "i8" else 0)
+    us = best[0]
+    return {"cu_num": torch.cuda.get_device_properties(0).multi_processor_count, "M": M, "N": N, "K": K,
+            "kernelName": best[1], "splitK": best[2], "us": round(us, 3),
+            "tflops": round(data.flops(M, N, K) / us / 1e6, 1), "bw": round(algo / us / 1e3, 1), "errRatio": 0,
+            "heuristic_kernelName": heur["kernelName"],
+            "heuristic_us": round(heur_row[0], 3) if heur_row else float("nan"),
+            "bad_plans": [r[1] for r in results if r[3] != 0.0], "plans": plans}
+
+
+def write_csv(rows: list, path: Path, planner: str = "fack_gemm_bs_plan") -> None:
     path.parent.mkdir(parents=True, exist_ok=True)
     with open(path, "w", newline="") as f:
-        f.write("# Exact-shape plans for fack_gemm_bs_plan, measured on B200 by python -m fack_b200.tune\n")
+        f.write(f"# Exact-shape plans for {planner}, measured on B200 by python -m fack_b200.tune\n")
         w = csv.DictWriter(f, fieldnames=HEADER, extrasaction="ignore")
         w.writeheader()
         for r in sorted(rows, key=lambda r: (r["N"], r["K"], r["M"])):
@@ -273,8 +399,10 @@ def parse_shapes(text: str) -> list:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--family", choices=["blockscale", "bf16", "i8", "siblings"], default="blockscale",
+                    help="the FP8 block-scaled GEMM (default) or the sibling BF16 / INT8 families (both: siblings)")
     ap.add_argument("--shapes", default="", help="M,N,K;M,N,K... (default: the tuned workloads)")
-    ap.add_argument("--out", default=str(_lib.TUNED_TABLE))
+    ap.add_argument("--out", default="", help="table to write (default: the family's table in configs/)")
     ap.add_argument("--log", default="", help="write every timed plan with the cost model's estimate (JSONL)")
     ap.add_argument("--report", default="", help="summarise a --log file (the model's regret per shape; no GPU)")
     ap.add_argument("--verbose", action="store_true")
@@ -288,21 +416,29 @@ def main(argv=None) -> int:
         print("tune: needs a CUDA device", file=sys.stderr)
         return 2
     lib = _lib.load()
-    lib.fack_gemm_bs_tuned_clear()  # time the cost model's plans, not an older table's
-    shapes = parse_shapes(args.shapes) if args.shapes else default_shapes()
+    sibling = args.family != "blockscale"
+    # time the cost model's plans, not an older table's
+    (lib.fack_gemm_tn_tuned_clear if sibling else lib.fack_gemm_bs_tuned_clear)()
+    out = args.out or str(_lib.TN_TUNED_TABLE if sibling else _lib.TUNED_TABLE)
+    if sibling:
+        families = SIBLING_FAMILIES if args.family == "siblings" else (args.family,)
+        shapes = parse_shapes(args.shapes) if args.shapes else sibling_default_shapes()
+        jobs = [(fam, s) for fam in families for s in shapes]
+    else:
+        jobs = [(None, s) for s in (parse_shapes(args.shapes) if args.shapes else default_shapes())]
     rows = []
     log = (lambda s: print(s, file=sys.stderr, flush=True)) if args.verbose else None
-    for M, N, K in shapes:
-        row = tune_shape(M, N, K, log)
+    for fam, (M, N, K) in jobs:
+        row = tune_sibling_shape(fam, M, N, K, log) if fam else tune_shape(M, N, K, log)
         rows.append(row)
         print(json.dumps({k: row[k] for k in ("M", "N", "K", "kernelName", "us", "heuristic_kernelName",
                                               "heuristic_us", "bad_plans")}), flush=True)
         torch.cuda.empty_cache()
-    write_csv(rows, Path(args.out))
+    write_csv(rows, Path(out), "fack_gemm_tn_plan" if sibling else "fack_gemm_bs_plan")
     if args.log:
         write_log(rows, Path(args.log))
     bad = sum(len(r["bad_plans"]) for r in rows)
-    print(json.dumps({"rows": len(rows), "out": args.out, "plans_failing_check": bad}))
+    print(json.dumps({"rows": len(rows), "out": out, "plans_failing_check": bad}))
     return 1 if bad else 0
 
 

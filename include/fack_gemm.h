@@ -178,6 +178,24 @@ int fack_gemm_bs_tuned_clear(void);
 int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skipped);
 
 /*
+ * The same exact-shape table for the sibling families (fack_gemm_tn): rows
+ * keyed by (kind = FACK_GEMM_BF16 | FACK_GEMM_I8, SM count, M, N, K) fix
+ * tile_m, tile_n and split_k of fack_gemm_tn_plan's fully automatic plan (all
+ * three requests 0).  Rows are checked by fack_gemm_tn_plan's rules for an
+ * explicit plan.  The CSV form is the FP8 table's, with kernelName
+ * fack_tn_sm100_{bf16|i8}_t{128|256}x{64|128|256}_s{S} (the name gives the
+ * kind); rows naming other kernels, the FP8 ones included, are skipped.
+ * _count / _clear touch the sibling rows only (and the FP8 functions the FP8
+ * rows only).
+ */
+int fack_gemm_tn_tuned_set(int kind, int cu_num, int M, int N, int K, int tile_m, int tile_n, int split_k);
+int fack_gemm_tn_tuned_lookup(int kind, int cu_num, int M, int N, int K, int* tile_m, int* tile_n,
+                              int* split_k);
+int fack_gemm_tn_tuned_count(void);
+int fack_gemm_tn_tuned_clear(void);
+int fack_gemm_tn_tuned_load(const char* path, int* rows_loaded, int* rows_skipped);
+
+/*
  * Bytes of workspace fack_gemm_bs needs for this problem and split (0 when the
  * plan has a single K slice).  Replaces the allocation the aiter launcher does
  * internally (csrc/py_itfs_cu/asm_a8w8_blockscale_bpreshuffle.cu, a missing
