@@ -4,7 +4,9 @@
 --pairs 8 --min-gain 0.01 --alpha 0.05``
 
 A version is either a build of the library (a path to a ``libfack_gemm.so``)
-or a plan of the current build (a kernel name ``fack_bs_sm100_t..x.._s..``).
+or a plan of the current build (a kernel name ``fack_bs_sm100_t..x.._s..``;
+with ``--family bf16|i8`` the sibling GEMMs are timed instead and plans are
+``fack_tn_sm100_{bf16|i8}_t..x.._s..``).
 Each trial times both versions on the same resident inputs, in alternating
 order (baseline first on even trials, candidate first on odd ones), and the
 pair of scores (1 / time) is reduced to a log ratio.  The verdict follows the
@@ -287,24 +289,44 @@ def run_pairs(evaluate: Callable[[str], Dict[str, float]], policy: dict, stage: 
 
 # ------------------------------------------------------------------ timing --
 
-class _Version:
-    """One side of a comparison: a library build and an optional fixed plan."""
+FAMILIES = ("blockscale", "bf16", "i8")
 
-    def __init__(self, spec: str):
-        from . import _lib, ops
-        self.plan = (0, 0, 0)
-        if spec.startswith(ops.KERNEL_PREFIX):
-            self.lib, self.plan = _lib.load(), ops.parse_kernel_name(spec)
+
+class _Version:
+    """One side of a comparison: a library build and an optional fixed plan,
+    for the FP8 block-scaled GEMM (``family="blockscale"``) or one of the
+    sibling families (``"bf16"``, ``"i8"``)."""
+
+    def __init__(self, spec: str, family: str = "blockscale"):
+        from . import _lib, ops, siblings
+        if family not in FAMILIES:
+            raise ValueError(f"family must be one of {FAMILIES}")
+        self.family, self.plan = family, (0, 0, 0)
+        prefix = ops.KERNEL_PREFIX if family == "blockscale" else siblings.PREFIX
+        if spec.startswith(ops.KERNEL_PREFIX) or spec.startswith(siblings.PREFIX):
+            if not spec.startswith(prefix):
+                raise ValueError(f"{spec}: not a plan of the {family} family ({prefix}_...)")
+            self.lib = _lib.load()
+            self.plan = (ops.parse_kernel_name(spec) if family == "blockscale"
+                         else siblings.parse_kernel_name(self.kind, spec))
         else:
             if not Path(spec).is_file():
-                raise ValueError(f"{spec}: neither a library file nor a {ops.KERNEL_PREFIX} kernel name")
+                raise ValueError(f"{spec}: neither a library file nor a {prefix} kernel name")
             self.lib = _lib.load(spec)  # another build, loaded beside the current one
-            if hasattr(self.lib, "fack_gemm_bs_tuned_load"):
-                for table in _lib.tuned_tables():
-                    _lib.load_tuned(table, self.lib)
+            sibling = family != "blockscale"
+            if hasattr(self.lib, "fack_gemm_tn_tuned_load" if sibling else "fack_gemm_bs_tuned_load"):
+                for table in _lib.tuned_tables(sibling=sibling):
+                    _lib.load_tuned(table, self.lib, sibling=sibling)
         self.spec = spec
 
+    @property
+    def kind(self) -> int:
+        from . import _lib
+        return _lib.FACK_GEMM_BF16 if self.family == "bf16" else _lib.FACK_GEMM_I8
+
     def launch(self, s, stream: int):
+        if self.family != "blockscale":
+            return self._launch_tn(s, stream)
         M, N, K = s["M"], s["N"], s["K"]
         tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
         st = self.lib.fack_gemm_bs_plan(M, N, K, *self.plan, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(sk),
@@ -317,23 +339,54 @@ class _Version:
         if st != 0:
             raise RuntimeError(f"{self.spec}: status {st}: {self.lib.fack_last_error().decode()}")
 
+    def _launch_tn(self, s, stream: int):
+        M, N, K = s["M"], s["N"], s["K"]
+        a, bp, sa, sb, out = s["cur"]
+        ptr = (lambda t: None if t is None else t.data_ptr())  # noqa: E731
+        st = self.lib.fack_gemm_tn(self.kind, a.data_ptr(), a.stride(0), bp.data_ptr(), 1, K, ptr(sa), ptr(sb),
+                                   None, out.data_ptr(), out.stride(0), M, N, K, *self.plan,
+                                   ctypes.c_void_p(stream))
+        if st != 0:
+            raise RuntimeError(f"{self.spec}: status {st}: {self.lib.fack_last_error().decode()}")
 
-def make_evaluator(baseline: str, candidate: str, shapes: List[tuple], launches: int = 24):
+
+def _input_sets(family: str, M: int, N: int, K: int, dev) -> list:
+    """Operand sets of one shape, together larger than 2.5 x the 126 MB L2."""
+    import torch
+    from . import data, ops
+    es = 2 if family == "bf16" else 1
+    sets = []
+    for i in range(max(1, math.ceil(2.5 * 126e6 / ((M + N) * K * es)))):
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        if family == "blockscale":
+            xq, xs = data.make_activations(M, K, "normal", 2 * i, dev)
+            wq, ws = data.make_weights(N, K, "normal", 2 * i + 1, dev)
+            sets.append((xq, data.to_aiter_xscale(xs), ops.shuffle_weight(wq), ws, out))
+            continue
+        g = torch.Generator(device=dev).manual_seed(i)
+        if family == "bf16":
+            a = (torch.randn((M, K), generator=g, device=dev) * 0.25).bfloat16()
+            b = (torch.randn((N, K), generator=g, device=dev) * 0.25).bfloat16()
+            sa = sb = None
+        else:
+            a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+            b = torch.randint(-128, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+            sa = 0.001 + 0.01 * torch.rand(M, generator=g, device=dev)
+            sb = 0.001 + 0.01 * torch.rand(N, generator=g, device=dev)
+        sets.append((a, ops.shuffle_weight(b), sa, sb, out))
+    return sets
+
+
+def make_evaluator(baseline: str, candidate: str, shapes: List[tuple], launches: int = 24,
+                   family: str = "blockscale"):
     """An ``evaluate(side)`` that times each shape's GEMM for one version
     (microseconds per call), the inputs shared by both versions."""
     import torch
-    from . import data, ops
-    versions = {"baseline": _Version(baseline), "candidate": _Version(candidate)}
+    versions = {"baseline": _Version(baseline, family), "candidate": _Version(candidate, family)}
     dev = torch.device("cuda")
     work = []
     for M, N, K in shapes:
-        per_set = M * K + N * K
-        sets = []
-        for i in range(max(1, math.ceil(2.5 * 126e6 / per_set))):
-            xq, xs = data.make_activations(M, K, "normal", 2 * i, dev)
-            wq, ws = data.make_weights(N, K, "normal", 2 * i + 1, dev)
-            sets.append((xq, data.to_aiter_xscale(xs), ops.shuffle_weight(wq), ws,
-                         torch.empty((M, N), dtype=torch.bfloat16, device=dev)))
+        sets = _input_sets(family, M, N, K, dev)
         work.append({"M": M, "N": N, "K": K, "sets": sets, "launches": max(launches, len(sets))})
     stream = torch.cuda.Stream()
 
@@ -367,8 +420,11 @@ def make_evaluator(baseline: str, candidate: str, shapes: List[tuple], launches:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("baseline", help="libfack_gemm.so path or fack_bs_sm100_t..x.._s.. plan")
-    ap.add_argument("candidate", help="libfack_gemm.so path or fack_bs_sm100_t..x.._s.. plan")
+    ap.add_argument("baseline", help="libfack_gemm.so path, or a plan: fack_bs_sm100_t..x.._s.. "
+                                     "(fack_tn_sm100_{bf16|i8}_t..x.._s.. with --family bf16|i8)")
+    ap.add_argument("candidate", help="libfack_gemm.so path or a plan of the same family")
+    ap.add_argument("--family", choices=FAMILIES, default="blockscale",
+                    help="the FP8 block-scaled GEMM (default) or a sibling family")
     ap.add_argument("--shape", action="append", required=True, help="M,N,K (repeatable)")
     ap.add_argument("--pairs", type=int, required=True, help="even, fixed pair count")
     ap.add_argument("--min-gain", type=float, required=True)
@@ -379,8 +435,8 @@ def main(argv=None) -> int:
               "min_gain": args.min_gain, "alpha": args.alpha, "max_confirmations": 1}
     validate_policy(policy)
     shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape]
-    report = run_pairs(make_evaluator(args.baseline, args.candidate, shapes), policy)
-    report.update(baseline=args.baseline, candidate=args.candidate)
+    report = run_pairs(make_evaluator(args.baseline, args.candidate, shapes, family=args.family), policy)
+    report.update(baseline=args.baseline, candidate=args.candidate, family=args.family)
     if args.out:
         Path(args.out).write_text(json.dumps(report, indent=2) + "\n")
     for name, r in report["results"].items():

@@ -165,3 +165,20 @@ def test_run_pairs_refuses_changing_timing_names():
 
     with pytest.raises(ValueError):
         ab.run_pairs(evaluate, sign_policy(8))
+
+
+def test_version_specs_per_family():
+    """Plans must belong to the compared family; library paths work for every family."""
+    from fack_b200 import _lib
+    v = ab._Version("fack_tn_sm100_i8_t128x256_s5", "i8")
+    assert v.plan == (128, 256, 5) and v.kind == _lib.FACK_GEMM_I8
+    assert ab._Version("fack_bs_sm100_t32x128_s5").plan == (32, 128, 5)
+    assert ab._Version(str(_lib.LIB_PATH), "bf16").plan == (0, 0, 0)
+    for spec, family in (("fack_tn_sm100_bf16_t128x256_s5", "blockscale"),   # sibling plan, FP8 comparison
+                         ("fack_bs_sm100_t128x256_s5", "i8"),                 # FP8 plan, sibling comparison
+                         ("fack_tn_sm100_bf16_t128x256_s5", "i8"),            # the other sibling
+                         ("fack_tn_sm100_i8_t256x256_s8", "i8"),              # pair: split <= 4
+                         ("/no/such/libfack_gemm.so", "bf16"),
+                         ("fack_bs_sm100_t128x256_s5", "fp4")):
+        with pytest.raises(ValueError):
+            ab._Version(spec, family)
