@@ -35,9 +35,15 @@ def load_golden(name):
     }
 
 
+def _nvidia_device_present() -> bool:
+    return any(Path(p).exists() for p in ("/dev/nvidiactl", "/dev/nvidia0"))
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     if not torch.cuda.is_available():
+        if _nvidia_device_present():  # a GPU machine whose CUDA does not work: fail, do not skip
+            pytest.fail("an NVIDIA device is present but CUDA is unavailable to torch", pytrace=False)
         pytest.skip("no CUDA device")
     cap = torch.cuda.get_device_capability(0)
     if cap != (10, 0):
