@@ -2,9 +2,9 @@
 // the same client (client/aiter/hsa/gfx942/gemm_driver.py), on B200 (sm_100a):
 //
 //   BF16 TN          Y[m,n] = bf16( sum_k A[m,k] * B[n,k]  (+ bias[n]) )
-//                    (gemm_driver.py:47-48: (a.float() @ b.float().T).bfloat16())
+//                    (gemm_driver.py:50: (a.float() @ b.float().T).bfloat16())
 //   INT8 per token   Y[m,n] = bf16( float(sum_k A[m,k] * B[n,k]) * sa[m] * sb[n] + bias[n] )
-//                    (gemm_driver.py:58-68: ((a.float() @ b.float().T) * sa * sb.T + bias))
+//                    (gemm_driver.py:73: ((a.float() @ b.float().T) * sa * sb.T + bias))
 //
 // Unlike the block-scaled FP8 path, nothing rescales between K blocks, so the
 // whole K range of a tile accumulates inside TMEM and the epilogue runs once:

@@ -237,7 +237,7 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     """Drop-in for aiter's ``gemm_a8w8_blockscale_bpreshuffle_asm`` (writes and returns ``out``).
 
     ``bias`` must be None: the blockscale operator has no bias term
-    (client/aiter/hsa/gfx942/dispatch_driver.py:66-67); ``zero_bias_buf`` is
+    (client/aiter/hsa/gfx942/dispatch_driver.py:65-66); ``zero_bias_buf`` is
     accepted and unused.  ``kernelName`` may be None, one of the reviewed
     gfx942 symbols (library choice of tile) or one of this library's names
     ``fack_bs_sm100_t{128|256}x{64|128|256}_s{S}`` (token tile 256 = a CTA
@@ -338,7 +338,7 @@ def shuffle_weight(b: torch.Tensor, layout=(16, 16)) -> torch.Tensor:
     """Pre-pack a ``[N, K]`` weight into this library's tile layout.
 
     Stand-in for aiter's ``shuffle_weight(b, layout=(16, 16))``
-    (client/aiter/hsa/gfx942/driver.py:21; gemm_driver.py:49, :67 for the
+    (client/aiter/hsa/gfx942/driver.py:21; gemm_driver.py:51, :74 for the
     sibling families).  e4m3, bf16 and int8 weights are accepted: the layout
     is defined on bytes -- 128-row x 128-byte tiles (128 e4m3 / int8 or 64
     bf16 elements of K) in their 128-byte-swizzled shared-memory image -- so

@@ -4,7 +4,7 @@ The reference drives two more GEMM families through the same client as the
 block-scaled FP8 path (client/aiter/hsa/gfx942/gemm_driver.py:32-79):
 
 * ``gemm_a16w16_asm(a, b, out, bias=None, splitK=None, kernelName=None,
-  bpreshuffle=False)`` -- BF16 TN, Y = bf16(A . B^T) (gemm_driver.py:53-54);
+  bpreshuffle=False)`` -- BF16 TN, Y = bf16(A . B^T) (gemm_driver.py:50, call :54);
 * ``gemm_a8w8_asm(a, b, sa, sb, out, kernelName=None, bias=None,
   bpreshuffle=True, splitK=None)`` -- INT8 with per-token activation scales
   ``sa`` [M, 1], per-channel weight scales ``sb`` [N, 1] and an fp32 bias
@@ -30,7 +30,7 @@ from . import _lib
 
 KINDS = {torch.bfloat16: _lib.FACK_GEMM_BF16, torch.int8: _lib.FACK_GEMM_I8}
 PREFIX = "fack_tn_sm100"
-# substrings of the reference's gfx942 catalog symbols (gemm_driver.py:45, :58)
+# substrings of the reference's gfx942 catalog symbols (gemm_driver.py:46, :58)
 AITER_PATTERNS = {_lib.FACK_GEMM_BF16: "bf16gemm_fp32bf16_", _lib.FACK_GEMM_I8: "I8gemm_bf16_perTokenI8_BpreShuffle_"}
 
 

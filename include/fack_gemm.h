@@ -325,11 +325,11 @@ int fack_quant_act(const void* x, int x_dtype, int64_t ldx, int M, int K, void* 
  * B[N,K] row-major, K contiguous), bf16 output Y[M,N] with row stride ldo:
  *
  *   kind = FACK_GEMM_BF16: Y = bf16(A . B^T (+ bias)), A and B bf16, fp32
- *     accumulation; a_scale and b_scale must be NULL (gemm_driver.py:47-48,
+ *     accumulation; a_scale and b_scale must be NULL (gemm_driver.py:50,
  *     aiter's gemm_a16w16_asm).
  *   kind = FACK_GEMM_I8: Y = bf16((float(A . B^T) * a_scale[m]) * b_scale[n]
  *     (+ bias[n])), A and B int8, exact s32 accumulation, each product and
- *     the sum rounded in fp32 in that order (gemm_driver.py:58-68, aiter's
+ *     the sum rounded in fp32 in that order (gemm_driver.py:73, aiter's
  *     gemm_a8w8_asm with per-token scales and an fp32 bias).
  *
  * lda / ldb / ldo are in elements; A and B rows 16-byte aligned (lda, ldb

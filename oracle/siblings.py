@@ -6,13 +6,13 @@ Only the tests and the benchmark's CPU legs may import it; the product path
 Restates the references of the reference's sibling driver,
 client/aiter/hsa/gfx942/gemm_driver.py:
 
-* BF16 TN (lines 45-48): ``(a.float() @ b.float().T).bfloat16()``;
-* INT8 per token (lines 58-68):
+* BF16 TN (line 50): ``(a.float() @ b.float().T).bfloat16()``;
+* INT8 per token (line 73):
   ``((a.float() @ b.float().T) * sa * sb.T + bias).bfloat16()`` with
   ``sa`` [M, 1], ``sb`` [N, 1] and ``bias`` [1, N] fp32.  The integer sum is
   formed exactly (int64) and rounded once to fp32, which equals the
   reference's fp32 matmul whenever that one is exact -- the driver's inputs
-  (|values| <= 16) guarantee it (gemm_driver.py:64).
+  (|values| <= 16) guarantee it (gemm_driver.py:60, :66, :69).
 
 Pinned by tests/golden/make_golden_siblings.py, which runs the driver's own
 ``prepare()`` and keeps its references.

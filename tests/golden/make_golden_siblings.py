@@ -11,7 +11,7 @@ exist:
   zeros); everything else is the real torch.
 
 ``prepare()`` then builds its inputs from its seeded generator and computes
-its own references (lines 47-48 for BF16, 58-68 for INT8) on the CPU.  Each
+its own references (line 50 for BF16, 73 for INT8) on the CPU.  Each
 case is saved as ``sib_<name>.npz``: a, b (bf16 as int16 bits / int8), and for
 INT8 sa, sb, bias and the padded row stride of a, plus the bf16 reference
 bits; ``index_siblings.json`` records the shapes and the driver's SHA-256.
@@ -35,7 +35,7 @@ HERE = Path(__file__).resolve().parent
 DEFAULT_REF = Path("/root/reference")
 SYMBOLS = {"bf16": "golden_bf16gemm_fp32bf16_tn", "i8": "golden_I8gemm_bf16_perTokenI8_BpreShuffle_tn"}
 
-# (name, family, m, n, k, bpreshuffle, seed); N % 64 (bf16) / % 256 (int8), K % 128 (gemm_driver.py:42-43)
+# (name, family, m, n, k, bpreshuffle, seed); N % 64 (bf16) / % 256 (int8), K % 128 (gemm_driver.py:41-42)
 CASES = [
     ("bf16_32x128x256", "bf16", 32, 128, 256, False, 11),
     ("bf16_ragged_33x192x384", "bf16", 33, 192, 384, False, 12),

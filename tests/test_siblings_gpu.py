@@ -65,7 +65,7 @@ def run_family(g, out, b, **kw):
 
 @pytest.mark.parametrize("name", sorted(INDEX))
 def test_golden_through_reference_call_form(cuda_device, name):
-    """gemm_driver.py:53-54 / :73 in spirit: splitK=1, a gfx942 symbol, the driver's bpreshuffle."""
+    """gemm_driver.py:54 / :77 in spirit: splitK=1, a gfx942 symbol, the driver's bpreshuffle."""
     g = load(name, cuda_device)
     shuffled = INDEX[name]["bpreshuffle"]
     b = fb.shuffle_weight(g["b"]) if shuffled else g["b"]
