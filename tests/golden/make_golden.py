@@ -40,7 +40,7 @@ SYMBOL = "_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_32x128E"
 # (name, m, n, k, seed): shapes the reference itself uses, plus edge cases.
 CASES = [
     ("manifest_256x256x1024", 256, 256, 1024, 123),   # client/aiter/hsa/gfx942/manifest.json:9, seed default 123
-    ("dispatch_192x1280x1024", 192, 1280, 1024, 987),  # unittests/test_aiter_dispatch.py:380 (contract shape)
+    ("dispatch_192x1280x1024", 192, 1280, 1024, 987),  # unittests/test_aiter_dispatch.py:378-381 (contract shape)
     ("min_1x128x128", 1, 128, 128, 0),                 # smallest legal problem
     ("ragged_33x384x640", 33, 384, 640, 7),            # M off every tile size, odd K/128
 ]
