@@ -65,6 +65,9 @@ enum fack_dtype {
   FACK_DTYPE_BF16 = 1    /* bf16                                               */
 };
 
+/* Status and version helpers: no counterpart in the reference, whose errors
+ * are Python exceptions (client/aiter/runner.py:208-212 reports them). */
+
 /* Human-readable text for a status code (static storage, never NULL). */
 const char* fack_status_string(int status);
 
@@ -114,7 +117,8 @@ int fack_gemm_bs_select(int M, int N, int K, int split_k_request,
  * SM cycles on the current device; 1e30 if the model would not offer it
  * (e.g. swapped small-M tiles whose clusters are not all resident at once).
  * For calibrating the model against measured times (python -m fack_b200.tune
- * --log); it launches nothing.
+ * --log); it launches nothing.  No counterpart in the reference, which
+ * chooses kernels from tuned tables only.
  */
 int fack_gemm_bs_plan_estimate(int M, int N, int K, int tile_m, int tile_n, int split_k, double* cycles);
 
@@ -130,6 +134,8 @@ int fack_gemm_bs_plan_estimate(int M, int N, int K, int tile_m, int tile_n, int 
  * ranks (e.g. a one-element all-reduce on the same stream): before it, so no
  * rank overwrites a Y another rank still reads; after it, so every rank's Y is
  * complete.  The kernel ends its peer stores with a system-scope fence.
+ * No counterpart in the reference, which runs one GPU per process with no
+ * collective (client/aiter/docs/validation.md:42-46).
  */
 int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
                        int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
@@ -141,7 +147,8 @@ int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packe
  * bytes into `handle`, handle_bytes >= 64) of the allocation holding `ptr` and
  * ptr's byte offset inside it (allocators hand out sub-ranges).  Another
  * process on the node opens the handle with fack_ipc_open_handle, adds the
- * offset, and releases it with fack_ipc_close_handle.
+ * offset, and releases it with fack_ipc_close_handle.  No counterpart in
+ * the reference (one GPU per process, no exchange between them).
  */
 int fack_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes, size_t* offset);
 int fack_ipc_open_handle(const void* handle, void** base);
@@ -178,7 +185,9 @@ int fack_gemm_bs_tuned_clear(void);
 int fack_gemm_bs_tuned_load(const char* path, int* rows_loaded, int* rows_skipped);
 
 /*
- * The same exact-shape table for the sibling families (fack_gemm_tn): rows
+ * The same exact-shape table for the sibling families (fack_gemm_tn), the
+ * counterpart of aiter's bf16 and a8w8 tuned GEMM tables that the reference
+ * names beside the blockscale one (client/aiter/dispatch.py:24-27): rows
  * keyed by (kind = FACK_GEMM_BF16 | FACK_GEMM_I8, SM count, M, N, K) fix
  * tile_m, tile_n and split_k of fack_gemm_tn_plan's fully automatic plan (all
  * three requests 0).  Rows are checked by fack_gemm_tn_plan's rules for an
@@ -353,7 +362,8 @@ int fack_gemm_tn(int kind, const void* a, int64_t lda, const void* b, int b_pack
  * Reads (and with reset != 0 clears) the current device's error word, which a
  * kernel sets when a bounded wait inside it gives up.  Synchronises `stream`.
  * *flags == 0 means no kernel has reported a problem.  Returns
- * FACK_ERR_DEVICE_TIMEOUT when flags are set, FACK_OK otherwise.
+ * FACK_ERR_DEVICE_TIMEOUT when flags are set, FACK_OK otherwise.  No
+ * counterpart in the reference (its kernels have no bounded waits to report).
  */
 int fack_device_status(void* stream, unsigned int* flags, int reset);
 
