@@ -53,6 +53,7 @@ namespace fack {
 
 constexpr int kBlk = 128;          // quantisation block along K and N
 constexpr int kTileM = 128;        // tokens per CTA (UMMA M, TMEM lanes)
+constexpr int kMaxM = 65535 * 128; // token tiles ride on gridDim.y (at most 65535)
 constexpr int kThreads = 384;      // 12 warps = 3 warpgroups
 constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..11 rescale and store
 constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
@@ -1287,6 +1288,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   const KernelEntry& k = kernel_for(tm, bn);
   int gx, gy, gz;
   plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
+  if (gy > 65535 || gz > 65535) return fail(FACK_ERR_BAD_SHAPE, "problem too large for one launch (grid y > 65535)");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gx, gy, gz);
   cfg.blockDim = dim3(k.threads, 1, 1);
@@ -1372,7 +1374,7 @@ const char* fack_last_error(void) { return g_last_error; }
 
 int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_request, int split_k_request,
                       int* tile_m, int* tile_n, int* split_k, size_t* workspace_bytes) {
-  if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk || M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
+  if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk || M > kMaxM) return FACK_ERR_BAD_SHAPE;
   if (!tile_m || !tile_n || !split_k) return FACK_ERR_BAD_ARG;
   const int KB = K / kBlk;
   if (split_k_request < 0 || split_k_request > kMaxSplit || split_k_request > KB) return FACK_ERR_BAD_ARG;
@@ -1466,7 +1468,7 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_outs)) return FACK_ERR_BAD_ARG;
   for (int i = 0; i < n_peers; ++i)
     if (!peer_outs[i] || !aligned(peer_outs[i], 16)) return FACK_ERR_BAD_ALIGN;
-  if (M > (1 << 24)) return FACK_ERR_BAD_SHAPE;
+  if (M > kMaxM) return FACK_ERR_BAD_SHAPE;
   if (wq_packed != FACK_W_ROW_MAJOR && wq_packed != FACK_W_PACKED) return FACK_ERR_BAD_ARG;
   if (!xq || !wq || !out || !x_scale || !w_scale) return FACK_ERR_BAD_ALIGN;
   if (!aligned(xq, 16) || !aligned(wq, 16) || !aligned(out, 16) || !aligned(x_scale, 4) || !aligned(w_scale, 4))

@@ -35,7 +35,7 @@ extern "C" {
 
 enum fack_status {
   FACK_OK = 0,
-  FACK_ERR_BAD_SHAPE = 1,       /* M<1, N or K not a positive multiple of 128 */
+  FACK_ERR_BAD_SHAPE = 1,       /* M<1 or M>8388480, N or K not a positive multiple of 128 */
   FACK_ERR_BAD_ALIGN = 2,       /* a pointer is NULL or misaligned */
   FACK_ERR_BAD_STRIDE = 3,      /* leading dimension / scale stride invalid */
   FACK_ERR_WS_TOO_SMALL = 4,    /* split-K workspace missing or too small */
@@ -232,6 +232,8 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale,
  * (client/aiter/hsa/gfx942/dispatch_driver.py:62-63; positional launch tuple
  * pinned at unittests/test_aiter_dispatch.py:504-505).
  *
+ *   M, N, K   1 <= M <= 8388480 (65535 tiles of 128 tokens); N and K positive
+ *             multiples of 128
  *   xq        e4m3 activations, row m at xq + m*ldx (ldx >= K, ldx % 16 == 0)
  *   wq        e4m3 weights, FACK_W_ROW_MAJOR ([N,K], row stride K) or
  *             FACK_W_PACKED (fack_gemm_bs_prepack_w output)

@@ -41,7 +41,8 @@ def test_status_strings_and_version():
     assert lib.fack_status_string(99).decode() == "unknown status"
 
 
-@pytest.mark.parametrize("m,n,k", [(0, 128, 128), (4, 100, 128), (4, 128, 100), (4, 0, 128), (4, 128, -128)])
+@pytest.mark.parametrize("m,n,k", [(0, 128, 128), (4, 100, 128), (4, 128, 100), (4, 0, 128), (4, 128, -128),
+                                   (65535 * 128 + 1, 128, 128)])   # more token tiles than gridDim.y holds
 def test_bad_shapes_rejected(m, n, k):
     lib = _lib.load()
     tm, sk = ctypes.c_int(), ctypes.c_int()

@@ -55,6 +55,7 @@ def test_set_lookup_replace_clear(lib):
     ((0, 256, 3072, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_ARG),     # cu_num
     ((148, 0, 3072, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),
     ((148, 256, 3000, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),
+    ((148, 65535 * 128 + 1, 3072, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),   # beyond 65535 token tiles
 ])
 def test_invalid_rows_refused(lib, row, status):
     assert lib.fack_gemm_bs_tuned_set(*row) == status
@@ -65,6 +66,10 @@ def write(tmp_path, text, name="t.csv"):
     p = tmp_path / name
     p.write_text(text)
     return p
+
+
+def test_largest_m_accepted(lib):
+    assert lib.fack_gemm_bs_tuned_set(148, 65535 * 128, 3072, 7168, 128, 256, 1) == 0
 
 
 def test_csv_load_by_column_name(lib, tmp_path):
