@@ -672,6 +672,7 @@ int fack_gemm_tn(int kind, const void* a, int64_t lda, const void* b, int b_pack
   const Entry& k = kernel_for(kind, tm, bn);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = plan_grid(M, N, tm, bn, sp);
+  if (cfg.gridDim.y > 65535 || cfg.gridDim.z > 65535) return FACK_ERR_BAD_SHAPE;  // beyond one launch's grid
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = static_cast<cudaStream_t>(stream);
