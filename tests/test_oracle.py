@@ -88,3 +88,18 @@ def test_small_generated_case_against_float64():
     y = orc.reference_gemm(xq, wq, xs, ws).double()
     exact = orc.exact_gemm_f64(xq, wq, xs, ws)
     assert torch.allclose(y, exact, rtol=1e-2, atol=1e-2)
+
+
+def test_outlier_and_uniform_activation_distributions():
+    """Prefill X: N(0,1) with 0.1 % of entries x50; wide-layer X: U(-1, 1).
+    Checked on the dequantised values (codes x per-group scale)."""
+    xq, xs = data.make_activations(512, 2048, "outlier", seed=5)
+    x = xq.float() * xs.repeat_interleave(128, dim=1)
+    big = int((x.abs() > 8).sum())              # a plain N(0,1) value beyond 8 has probability ~1e-15
+    expected = x.numel() * 1e-3 * 0.873          # P(|50 z| > 8) = P(|z| > 0.16) = 0.873
+    assert 0.8 * expected < big < 1.2 * expected, (big, expected)
+    assert float(x.abs().max()) > 100            # some outliers reach several sigma x 50
+    xq, xs = data.make_activations(64, 2048, "uniform", seed=6)
+    x = xq.float() * xs.repeat_interleave(128, dim=1)
+    assert float(x.abs().max()) <= 1.0 and abs(float(x.mean())) < 0.02
+    assert abs(float((x.abs() < 0.5).float().mean()) - 0.5) < 0.02
