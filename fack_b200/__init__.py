@@ -21,13 +21,15 @@ from .ops import (  # noqa: F401
     shuffle_weight,
     workspace_size,
 )
-from .siblings import gemm_a8w8_asm, gemm_a16w16_asm, gemm_tn  # noqa: F401
+from .siblings import gemm_a8w8_ASM, gemm_a8w8_asm, gemm_a16w16, gemm_a16w16_asm, gemm_tn  # noqa: F401
 
 __all__ = [
     "AITER_SYMBOLS",
     "device_status",
     "gather_interleave",
+    "gemm_a16w16",
     "gemm_a16w16_asm",
+    "gemm_a8w8_ASM",
     "gemm_a8w8_asm",
     "gemm_tn",
     "gemm_a8w8_blockscale_bpreshuffle",

@@ -147,3 +147,45 @@ def gemm_a8w8_asm(a, b, sa, sb, out, kernelName=None, bias=None, bpreshuffle=Tru
     flat = lambda t: None if t is None else t.reshape(-1)  # noqa: E731  ([M,1] / [N,1] / [1,N] views)
     return gemm_tn(a, b, out, a_scale=flat(sa), b_scale=flat(sb), bias=flat(bias), packed=shuffled,
                    tile_n=tile_n, split_k=split, tile_m=tile_m)
+
+
+def _public_plan(kind: int, a, b, name: str):
+    """(M, N, K, config) for a public entry, after the checks that need no device."""
+    for nm, t in (("a", a), ("b", b)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dim() != 2:
+            raise ValueError(f"{name}: {nm} must be a 2-D CUDA tensor")
+    M, K = a.shape
+    N = b.shape[0]
+    with torch.cuda.device(a.device):
+        return M, N, K, get_config(kind, M, N, K)
+
+
+def gemm_a8w8_ASM(a, b, sa, sb, bias=None, dtype=torch.bfloat16):
+    """Drop-in for aiter's public INT8 entry ``gemm_a8w8_ASM`` (the call the
+    reference's dispatch check makes, client/aiter/hsa/gfx942/dispatch_driver.py:55-56):
+    picks the plan for (M, N, K) (exact-shape table first, then the cost
+    model), allocates ``out`` and makes one :func:`gemm_a8w8_asm` call with
+    that kernelName and splitK."""
+    if dtype != torch.bfloat16:
+        raise ValueError("only bfloat16 output is supported")
+    if not isinstance(a, torch.Tensor) or a.dtype != torch.int8:
+        raise ValueError("gemm_a8w8_ASM takes int8 operands")
+    M, N, K, cfg = _public_plan(KINDS[torch.int8], a, b, "gemm_a8w8_ASM")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    return gemm_a8w8_asm(a, b, sa, sb, out, kernelName=cfg["kernelName"], bias=bias,
+                         bpreshuffle=bool(getattr(b, "is_shuffled", False)), splitK=cfg["splitK"])
+
+
+def gemm_a16w16(a, b, bias=None, otype=torch.bfloat16):
+    """Drop-in for aiter's public BF16 entry ``tuned_gemm.gemm_a16w16`` (the
+    call the reference's dispatch check makes,
+    client/aiter/hsa/gfx942/dispatch_driver.py:86-87): picks the plan,
+    allocates ``out`` and makes one :func:`gemm_a16w16_asm` call."""
+    if otype != torch.bfloat16:
+        raise ValueError("only bfloat16 output is supported")
+    if not isinstance(a, torch.Tensor) or a.dtype != torch.bfloat16:
+        raise ValueError("gemm_a16w16 takes bfloat16 operands")
+    M, N, K, cfg = _public_plan(KINDS[torch.bfloat16], a, b, "gemm_a16w16")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    return gemm_a16w16_asm(a, b, out, bias=bias, splitK=cfg["splitK"], kernelName=cfg["kernelName"],
+                           bpreshuffle=bool(getattr(b, "is_shuffled", False)))

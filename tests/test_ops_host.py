@@ -107,3 +107,22 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
         _lib.load()
     with pytest.raises(RuntimeError, match="no fallback"):
         fb.get_config(256, 3072, 7168)
+
+
+def test_public_sibling_entries_refuse_before_any_device_query():
+    """gemm_a8w8_ASM / gemm_a16w16 (dispatch_driver.py:55-56, :86-87)."""
+    a8, b8 = torch.zeros(4, 256, dtype=torch.int8), torch.zeros(256, 256, dtype=torch.int8)
+    s4, s256 = torch.ones(4, 1), torch.ones(256, 1)
+    with pytest.raises(ValueError, match="bfloat16 output"):
+        fb.gemm_a8w8_ASM(a8, b8, s4, s256, dtype=torch.float16)
+    with pytest.raises(ValueError, match="int8 operands"):
+        fb.gemm_a8w8_ASM(a8.float(), b8, s4, s256)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        fb.gemm_a8w8_ASM(a8, b8, s4, s256)
+    abf, bbf = torch.zeros(4, 256, dtype=torch.bfloat16), torch.zeros(256, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="bfloat16 output"):
+        fb.gemm_a16w16(abf, bbf, otype=torch.float32)
+    with pytest.raises(ValueError, match="bfloat16 operands"):
+        fb.gemm_a16w16(a8, bbf)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        fb.gemm_a16w16(abf, bbf)

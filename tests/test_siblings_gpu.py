@@ -166,6 +166,26 @@ def test_split_k_bitwise_reproducible_and_strided_out(cuda_device):
     assert torch.isnan(big[:, :32].float()).all() and torch.isnan(big[:, 32 + 1024:].float()).all()
 
 
+@pytest.mark.parametrize("name", sorted(INDEX))
+def test_public_entries_one_asm_call(cuda_device, name):
+    """gemm_a8w8_ASM / gemm_a16w16 (dispatch_driver.py:55-56, :86-87): the
+    library's plan, a fresh output, the same bits as the asm-level entry."""
+    g = load(name, cuda_device)
+    d = cuda_device
+    packed = g["n"] % 128 == 0
+    b = fb.shuffle_weight(g["b"]) if packed else g["b"]
+    want = poisoned(g["m"], g["n"], d)
+    if g["fam"] == "bf16":
+        y = fb.gemm_a16w16(g["a"], b, bias=None, otype=torch.bfloat16)
+        fb.gemm_a16w16_asm(g["a"], b, want, bpreshuffle=packed)
+    else:
+        y = fb.gemm_a8w8_ASM(g["a"], b, g["sa"], g["sb"], bias=g["bias"], dtype=torch.bfloat16)
+        fb.gemm_a8w8_asm(g["a"], b, g["sa"], g["sb"], want, bias=g["bias"], bpreshuffle=packed)
+    assert y.shape == (g["m"], g["n"]) and y.dtype == torch.bfloat16
+    check(y, g["reference"], g["fam"] == "i8", name + " public")
+    assert torch.equal(y.view(torch.int16), want.view(torch.int16))
+
+
 def test_public_config_and_contract_errors(cuda_device):
     cfg = siblings.get_config(siblings.KINDS[torch.int8], 256, 3072, 7168)
     assert cfg["kernelName"].startswith("fack_tn_sm100_i8_t") and cfg["splitK"] >= 1
