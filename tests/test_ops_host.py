@@ -126,3 +126,10 @@ def test_public_sibling_entries_refuse_before_any_device_query():
         fb.gemm_a16w16(a8, bbf)
     with pytest.raises(ValueError, match="CUDA tensor"):
         fb.gemm_a16w16(abf, bbf)
+
+
+def test_quantize_activations_refuses_before_launch():
+    with pytest.raises(ValueError, match="CUDA"):
+        fb.quantize_activations(torch.zeros(4, 256))
+    with pytest.raises(ValueError, match="2-D"):
+        fb.quantize_activations(torch.zeros(256))
