@@ -4,22 +4,25 @@
 Metric: FP8 blockscale GEMM TFLOPS (2*M*N*K per call), with HBM GB/s and the
 roofline fraction of the GEMM kernel, and us/call.
 
-Default workload: the single-GPU decode shape M=256, N=3072, K=7168 (fp32
-block scales, e4m3 operands, bf16 output), called exactly as the reference's
-timed run does -- pre-packed weight, transposed-contiguous x_scale,
-``gemm_a8w8_blockscale_bpreshuffle_asm(a, packed_b, out, packed_sa, sb, ...)``
-(client/aiter/hsa/gfx942/driver.py:26-29).  A step is one call on one input
-set; steps rotate over enough distinct input sets that the rotation exceeds
-2.5x the 126 MB L2, and are timed as CUDA-graph replays with CUDA events
-(client/aiter/runner.py:160-189 times graph replays the same way).
+Default workload: the prefill layer M=8192, N=7168, K=16384 (e4m3 operands,
+fp32 block scales, bf16 output), the configuration the benchmark quotes at
+1, 2, 4 and 8 GPUs.  At N=1 a step is one call of the reference's timed
+operator, ``gemm_a8w8_blockscale_bpreshuffle_asm(a, packed_b, out, packed_sa,
+sb, ...)`` (client/aiter/hsa/gfx942/driver.py:26-29: pre-packed weight,
+transposed-contiguous x_scale).  Under torchrun (``--gpus N``) the output
+columns are sharded over the ranks (strong scaling): rank r holds WQ rows
+[r*N/g, (r+1)*N/g), and each step is one launch per rank whose epilogue
+stores every bf16 tile into every rank's Y over NVLink peer mappings and
+whose last CTA completes the exchange on the device (``--gather fused``,
+the default), or the blocks are all-gathered over NCCL and interleaved
+(``--gather nccl``).  The decode shape M=256, N=3072, K=7168 is measured
+beside it on every rank (key ``decode``) and can be the headline with
+``--workload decode``; ``--workload`` selects any benchmark config.
 
-``--gpus N`` under torchrun: the decode / plumbing / sweep workloads do not
-shard, so N ranks run N independent replicas (weak scaling, no collective).
-``--workload prefill|wide_constant|wide_uniform`` shards the output columns
-over the ranks (strong scaling); every step each rank's GEMM epilogue stores
-its bf16 column block into every rank's Y over NVLink peer mappings, between
-two one-element NCCL all-reduces (``--gather fused``, the default), or the
-blocks are all-gathered over NCCL and interleaved (``--gather nccl``).
+Steps rotate over enough distinct input sets that the rotation exceeds 2.5x
+the 126 MB L2 (one set when a set alone is larger), and are timed as
+CUDA-graph replays with CUDA events on the launch stream, max over ranks
+(client/aiter/runner.py:160-189 times graph replays the same way).
 
 ``--impl reference`` times the reference's own algorithm for this path -- the
 fp32 dequantise-then-matmul of client/aiter/hsa/gfx942/driver.py:18-20 -- on
@@ -232,6 +235,77 @@ def cpu_oracle_rate(wl, budget_s: float, max_steps: int = 3):
 
 
 # ------------------------------------------------------------- our arm --
+def roofline(k_bytes, k_flops, k_us, peaks, clk, region_ms):
+    """Roofline of one GEMM launch of k_us: the bound (HBM or tensor) whose
+    time is the larger.  The tensor peak that applies is the one at the clocks
+    the timed region ran at: the burst GEMM figure while the SM clock held its
+    maximum, the sustained (power-capped) figure once it dropped below 95 % of
+    it; without clock samples, the sustained figure for a region over 0.2 s."""
+    if clk and clk.get("samples") and clk.get("sm_mhz") and clk.get("sm_max_mhz"):
+        sustained = clk["sm_mhz"] < 0.95 * clk["sm_max_mhz"]
+        why = f"median SM clock {clk['sm_mhz']:.0f} of {clk['sm_max_mhz']} MHz"
+    else:
+        sustained = region_ms > 200.0
+        why = f"timed region {region_ms:.0f} ms"
+    bf16_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    fp8_peak = 2.0 * bf16_peak
+    t_mem = k_bytes / (peaks["hbm_gbs"] * 1e3)        # us
+    t_tc = k_flops / (fp8_peak * 1e6)                 # us
+    hbm_gbs = k_bytes / (k_us * 1e3)
+    tflops_k = k_flops / (k_us * 1e6)
+    if t_mem >= t_tc:
+        roof = {"bound": "hbm", "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(hbm_gbs / peaks["hbm_gbs"], 4)}
+    else:
+        roof = {"bound": "tensor", "achieved": round(tflops_k, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                "frac": round(tflops_k / fp8_peak, 4)}
+    roof.update({"algorithmic_bytes": k_bytes, "kernel_us": round(k_us, 3), "peak_source": (
+        f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 "
+        f"{'sustained' if sustained else 'burst'} {bf16_peak} TFLOP/s ({why})"),
+        "t_mem_us": round(t_mem, 3), "t_tc_us": round(t_tc, 3),
+        "frac_of_max_roof": round(max(t_mem, t_tc) / k_us, 4)})
+    return roof
+
+
+def measure_unsharded(name, steps, dev, stream, world, peaks, clk):
+    """Kernel time of an unsharded workload on this rank's GPU (replicas when
+    world > 1): CUDA-graph replays of the reference's call form over rotating
+    input sets, max over ranks.  The secondary record of the bench line."""
+    import fack_b200 as fb
+    from fack_b200 import data
+    wl = data.WORKLOADS[name]
+    set_bytes = data.algorithmic_bytes(wl.M, wl.N, wl.K)
+    n_sets = max(1, math.ceil(2.5 * L2_BYTES / set_bytes))
+    sets = make_sets(wl, n_sets, dev, None)
+    cfg = fb.get_config(wl.M, wl.N, wl.K)
+
+    def call(s):
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(s["a"], s["b"], s["out"], s["sa"], s["sb"], None,
+                                                cfg["splitK"], cfg["kernelName"], True)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            call(sets[i % n_sets])
+    torch.cuda.synchronize(dev)
+    chunk = n_sets * max(1, 256 // n_sets)
+    graphs = []
+    with torch.cuda.stream(stream):
+        run = capture(lambda: [call(sets[i % n_sets]) for i in range(chunk)], stream, graphs)
+    reps = max(3, math.ceil(steps / chunk))
+    timed_graph_replay([(run, 2)], stream)
+    barrier(world)
+    ms = max_over_ranks(timed_graph_replay([(run, reps)], stream), world, dev)
+    for g in graphs:
+        g.reset()
+    us = ms * 1e3 / (reps * chunk)
+    roof = roofline(set_bytes, data.flops(wl.M, wl.N, wl.K), us, peaks, clk, ms)
+    del sets
+    return {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "kernel": cfg["kernelName"],
+            "us_per_call": round(us, 3), "tflops": round(data.flops(wl.M, wl.N, wl.K) / (us * 1e6), 2),
+            "hbm_gbs": round(set_bytes / (us * 1e3), 1), "calls_timed": reps * chunk,
+            "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB", "roofline": roof,
+            "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+
+
 def run_ours(args):
     import fack_b200 as fb
     from fack_b200 import data
@@ -254,7 +328,9 @@ def run_ours(args):
     if sharded:
         from fack_b200.dist import ShardedBlockscaleGemm
         sharder = ShardedBlockscaleGemm(mode=args.gather)
-        full_out = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(n_sets)]
+        # two outputs alternate, so a peer never stores into the Y of the
+        # step before (the fused path then needs no extra exchange step)
+        full_out = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
 
     def gemm_call(s):
         fb.gemm_a8w8_blockscale_bpreshuffle_asm(s["a"], s["b"], s["out"], s["sa"], s["sb"], None,
@@ -263,18 +339,21 @@ def run_ours(args):
     def step(i):
         s = sets[i % n_sets]
         if sharded:
-            sharder(s["a"], s["b"], s["sa_logical"], s["sb"], out=full_out[i % n_sets])
+            sharder(s["a"], s["b"], s["sa_logical"], s["sb"], out=full_out[i % 2])
         else:
             gemm_call(s)
 
     log(f"[bench rank {rank}] {wl.name}: {n_sets} input sets, plan {cfg['kernelName']}, sharded={sharded}")
-    # warm-up (eager: sizes the split-K workspace and the gather buffer)
+    # warm-up (eager: sizes the split-K workspace, registers the outputs and
+    # the exchange state); an even count ends on the second output
+    warm = args.warmup + (args.warmup % 2)
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
+        for i in range(warm):
             step(i)
     barrier(world)
 
-    chunk = max(n_sets, (min(args.steps, 1024) // n_sets) * n_sets)
+    period = n_sets if n_sets % 2 == 0 else 2 * n_sets   # a graph starts on output 0 and set 0
+    chunk = max(period, (min(args.steps, 1024) // period) * period)
     full, rem = divmod(args.steps, chunk)
     graphs = []
     timing = "CUDA-graph replay"
@@ -298,7 +377,7 @@ def run_ours(args):
         timing = "eager launches"
         run_chunk, run_rem = steps_fn(chunk), steps_fn(rem)
         run_gemm = gemm_fn(chunk) if sharded else None
-    if world > 1:  # all ranks must time the same way (captured steps hold collectives)
+    if world > 1:  # all ranks must time the same way (captured steps hold exchange steps)
         flag = torch.tensor([1 if graphs else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if flag.item() == 0 and graphs:
@@ -317,8 +396,8 @@ def run_ours(args):
     sampler = ClockSampler(local)
     sampler.start()
     probe = run_chunk or run_rem
-    # every rank must replay the same number of steps (the sharded steps hold
-    # collectives), so the warm-up count comes from the slowest rank's probe
+    # every rank must replay the same number of steps (the sharded steps wait
+    # on each other), so the warm-up count comes from the slowest rank's probe
     t_probe = max_over_ranks(timed_graph_replay([(probe, 1)], stream) / 1e3, world, dev)
     log(f"[bench rank {rank}] probe {t_probe * 1e3:.3f} ms per chunk; warming, then timing {args.steps} steps")
     timed_graph_replay([(probe, max(1, int(0.3 / max(t_probe, 1e-6))))], stream)
@@ -327,13 +406,15 @@ def run_ours(args):
     sampler.stop()
     barrier(world)
     ms = max_over_ranks(ms, world, dev)
+    clk = sampler.summary()
 
     us_call = ms * 1e3 / args.steps
     ranks_work = world if not sharded else 1
     total_flops = data.flops(wl.M, wl.N, wl.K) * ranks_work * args.steps
     value = total_flops / (ms / 1e3) / 1e12
 
-    # roofline of the GEMM kernel (per launch on one GPU)
+    # roofline of the GEMM kernel (per launch on one GPU): for a sharded step
+    # the same rank's launch without peer stores or exchange, timed alone
     if sharded:
         k_ms = timed_graph_replay([(run_gemm, 1)], stream)
         k_us = max_over_ranks(k_ms * 1e3 / chunk, world, dev)
@@ -341,84 +422,67 @@ def run_ours(args):
         k_us = us_call
     peaks = measured_peaks()
     k_bytes = data.algorithmic_bytes(wl.M, n_local, wl.K)
-    k_flops = data.flops(wl.M, n_local, wl.K)
-    # The tensor peak that applies is the one at the clocks the timed region
-    # ran at: the burst GEMM figure while the SM clock held its maximum, the
-    # sustained (power-capped) figure once it dropped below 95 % of it.
-    # Without clock samples: the sustained figure for a region over ~0.2 s.
-    clk = sampler.summary()
-    if clk and clk.get("samples") and clk.get("sm_mhz") and clk.get("sm_max_mhz"):
-        sustained = clk["sm_mhz"] < 0.95 * clk["sm_max_mhz"]
-        why = f"median SM clock {clk['sm_mhz']:.0f} of {clk['sm_max_mhz']} MHz"
-    else:
-        sustained = ms > 200.0
-        why = f"timed region {ms:.0f} ms"
-    bf16_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
-    fp8_peak = 2.0 * bf16_peak
-    t_mem = k_bytes / (peaks["hbm_gbs"] * 1e3)        # us
-    t_tc = k_flops / (fp8_peak * 1e6)                 # us
-    hbm_gbs = k_bytes / (k_us * 1e3)
-    tflops_k = k_flops / (k_us * 1e6)
-    if t_mem >= t_tc:
-        roof = {"bound": "hbm", "achieved": round(hbm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(hbm_gbs / peaks["hbm_gbs"], 4)}
-    else:
-        roof = {"bound": "tensor", "achieved": round(tflops_k, 1), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                "frac": round(tflops_k / fp8_peak, 4)}
-    # ncu DRAM bytes of the workload's single-GPU launch; a column shard reads
-    # its share of the weights (they are all but ~1 % of the bytes), so its
-    # launch is scaled by n_local / N
+    roof = roofline(k_bytes, data.flops(wl.M, n_local, wl.K), k_us, peaks, clk, ms)
+    roof["step_us"] = round(us_call, 3)
+    # ncu DRAM bytes of the workload's launch on one GPU; a column shard reads
+    # its share of the weights and writes its share of Y, so its launch is
+    # reported as that scaled by n_local / N
     traffic = load_traffic(args.workload)
     if traffic is not None and sharded:
         traffic = int(round(traffic * n_local / wl.N))
-    roof.update({"traffic": traffic, "algorithmic_bytes": k_bytes,
-                 "kernel_us": round(k_us, 3), "peak_source": (
-                     f"{peaks['source']} MEASURED_PEAKS.json: hbm_gbs copy bandwidth; fp8 dense = 2 x bf16 "
-                     f"{'sustained' if sustained else 'burst'} {bf16_peak} TFLOP/s ({why})"),
-                 "t_mem_us": round(t_mem, 3), "t_tc_us": round(t_tc, 3),
-                 "frac_of_max_roof": round(max(t_mem, t_tc) / k_us, 4)})
+    roof = {**{k: roof[k] for k in ("bound", "achieved", "peak", "unit", "frac")}, "traffic": traffic,
+            **{k: v for k, v in roof.items() if k not in ("bound", "achieved", "peak", "unit", "frac")}}
 
     # e2e through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, wl, sets[0], dev, stream, sharder, world)
+        e2e = run_e2e(args, wl, sets[0], dev, stream, sharder, world, cfg)
+
+    # the decode shape beside the headline (replicas at N > 1)
+    decode = None
+    if args.workload != "decode" and not args.no_decode:
+        del sets
+        torch.cuda.empty_cache()
+        decode = measure_unsharded("decode", 2000, dev, stream, world, peaks, clk)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tfl, cores, sample = cpu_oracle_rate(wl, budget_s=args.cpu_budget)
         cpu = {"value": round(tfl, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample}
 
-    clocks = sampler.summary()
-    # GEMM (+ the column interleave of the NCCL-gather path); the fused path's
-    # two one-element all-reduces per step are NCCL's kernels, not counted
+    # GEMM launches per step: one (its last CTA runs the fused exchange), plus
+    # the interleave of the NCCL-gather path (NCCL's own kernels not counted)
     per_step_launches = 2 if sharded and args.gather == "nccl" else 1
+    extra = sharder.barriers if sharder is not None and args.gather == "fused" else 0
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 6), "higher_is_better": True,
-        "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate, bf16 out)",
+        "scaling": "strong" if sharded or args.workload in SHARDED else "weak", "vs_baseline": None,
+        "dtype": "fp8_e4m3 (fp32 accumulate, bf16 out)",
         "data": "synthetic (seeded; benchmark-config construction, scale = amax/240)",
         "config": {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "M": wl.M, "N": wl.N, "K": wl.K,
                    "x_dist": wl.x_dist, "w_dist": wl.w_dist, "tile_m": cfg["tile_m"], "split_k": cfg["splitK"],
-                   "kernel": cfg["kernelName"], "weights": "prepacked (bpreshuffle=True)",
+                   "kernel": cfg["kernelName"], "n_local": n_local, "weights": "prepacked (bpreshuffle=True)",
                    "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB = {n_sets * set_bytes / 1e6:.0f} MB"
                          f" (> 126 MB L2)",
                    "timing": f"{timing}, CUDA events on the launch stream, max over ranks",
-                   "parallelism": ((f"N-shard g={world}: GEMM epilogue stores every tile to all ranks' Y over "
-                                    "NVLink peer mappings (CUDA IPC), 1-element NCCL all-reduce barriers"
+                   "parallelism": ((f"N-shard g={world}: one launch per rank per step; its epilogue stores every "
+                                    "tile to all ranks' Y over NVLink peer mappings (CUDA IPC) and its last CTA "
+                                    "signals the peers and waits for theirs (no collective on the stream)"
                                     if args.gather == "fused" else f"N-shard g={world} + NCCL all-gather")
                                    if sharded else
                                    ("single GPU" if world == 1 else f"{world} independent replicas"))},
-        "us_per_call": round(us_call, 3), "hbm_gbs": round(data.algorithmic_bytes(wl.M, n_local, wl.K) /
-                                                           (k_us * 1e3), 1),
-        "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "us_per_call": round(us_call, 3), "hbm_gbs": round(k_bytes / (k_us * 1e3), 1),
+        "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "decode": decode,
         "gpu_launches": per_step_launches * args.steps,
+        "gpu_launches_note": f"{extra} stand-alone exchange steps outside the timed region" if extra else None,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     status = fb.device_status()
     if status:
         log(f"device status flags set: {status:#x}")
-    for g in graphs:  # graphs holding NCCL work must go before the process group
+    for g in graphs:
         g.reset()
     del graphs, plan, probe, run_chunk, run_rem, run_gemm
     if world > 1:
@@ -432,113 +496,98 @@ def run_ours(args):
         sys.exit(3)
 
 
-def run_e2e(args, wl, s0, dev, stream, sharder, world):
-    """Public API, host inputs: per step H2D of XQ + x_scale (pinned), the call, D2H of Y."""
+def run_e2e(args, wl, s0, dev, stream, sharder, world, cfg):
+    """Public API, host inputs: per step the pinned H2D of XQ + x_scale, the
+    call, the D2H of Y, on three streams over rotating buffers (step i's
+    inputs cross PCIe while step i-1 computes and step i-2's result comes
+    back; each step still moves its own bytes), captured in CUDA graphs as the
+    reference's runner captures its timed launches (client/aiter/runner.py:
+    169-172), at least three graphs."""
     import fack_b200 as fb
-    steps = min(args.steps, args.e2e_steps)
+    from fack_b200 import data
     a_h = s0["a"].cpu().pin_memory()
     sa_h = (s0["sa_logical"] if sharder else s0["sa"]).cpu().pin_memory()
-    n_out = wl.N
-    y_h = torch.empty((wl.M, n_out), dtype=torch.bfloat16).pin_memory()
-    a_d = torch.empty_like(s0["a"])
-    sa_d = torch.empty_like(s0["sa"])
-    full = torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) if sharder else None
+    y_h = torch.empty((wl.M, wl.N), dtype=torch.bfloat16).pin_memory()
+    h2d = a_h.numel() * a_h.element_size() + sa_h.numel() * 4
+    d2h = y_h.numel() * 2
+    # outputs rotate over nb buffers; GEMM i waits for the copy-out of step
+    # i - w.  Sharded: a peer stores into buffer i % 3 once every rank has
+    # finished step i - 1, whose GEMM waited for the copy-out of step i - 3,
+    # the buffer's previous use.
+    nb, w = (3, 2) if sharder else (2, 2)
+    per_graph = 64 if h2d + d2h < 32e6 else 15
+    per_graph -= per_graph % nb
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    a_b = [torch.empty_like(s0["a"]) for _ in range(2)]
+    sa_b = [torch.empty_like(sa_h, device=dev) for _ in range(2)]
+    out_b = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(nb)]
 
-    def one():
-        a_d.copy_(a_h, non_blocking=True)
-        sa_d.copy_(sa_h, non_blocking=True)
+    def call(i, b, o):
         if sharder:
-            y = sharder(a_d, s0["b"], sa_d, s0["sb"], out=full)
+            sharder(a_b[b], s0["b"], sa_b[b], s0["sb"], out=out_b[o])
         else:
-            y = fb.gemm_a8w8_blockscale_bpreshuffle(a_d, s0["b"], sa_d, s0["sb"], dtype=torch.bfloat16)
-        y_h.copy_(y, non_blocking=True)
+            fb.gemm_a8w8_blockscale_bpreshuffle_asm(a_b[b], s0["b"], out_b[o], sa_b[b], s0["sb"], None,
+                                                    cfg["splitK"], cfg["kernelName"], True)
 
-    # Unsharded: each step's copy-in, call and copy-out on three streams over two
-    # device buffers, so step i's inputs cross PCIe while step i-1 computes and
-    # step i-2's result comes back (each step still moves its own bytes); the
-    # steps are captured in CUDA graphs of `per_graph` steps, as the
-    # reference's runner captures its timed launches (client/aiter/runner.py:
-    # 169-172), so host-side Python does not pace the pipeline.  The call is the
-    # reference's timed operator, gemm_a8w8_blockscale_bpreshuffle_asm, with a
-    # caller-owned output and the plan the public entry selects.  The sharded
-    # call holds collectives on its stream and stays sequential.
-    pipelined = sharder is None
+    def steps_graph(n):
+        fork = torch.cuda.Event()
+        fork.record(stream)                        # the side streams join the capture here
+        s_in.wait_event(fork)
+        s_out.wait_event(fork)
+        comp, outd, ev_in = [], [], None
+        for i in range(n):
+            b, o = i % 2, i % nb
+            if i >= 2:
+                s_in.wait_event(comp[i - 2])       # step i-2's call has read these inputs
+            ev_in = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                a_b[b].copy_(a_h, non_blocking=True)
+                sa_b[b].copy_(sa_h, non_blocking=True)
+                ev_in.record(s_in)
+            stream.wait_event(ev_in)
+            if i >= w:
+                stream.wait_event(outd[i - w])
+            call(i, b, o)
+            ev_c = torch.cuda.Event()
+            ev_c.record(stream)
+            comp.append(ev_c)
+            s_out.wait_event(ev_c)
+            ev_o = torch.cuda.Event()
+            with torch.cuda.stream(s_out):
+                y_h.copy_(out_b[o], non_blocking=True)
+                ev_o.record(s_out)
+            outd.append(ev_o)
+        stream.wait_event(outd[-1])                # join both side streams back
+        stream.wait_event(ev_in)
+
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if pipelined:
-        cfg = fb.get_config(wl.M, wl.N, wl.K)
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        a_b = [a_d, torch.empty_like(a_d)]
-        sa_b = [sa_d, torch.empty_like(sa_d)]
-        out_b = [torch.empty((wl.M, wl.N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-        y_hb = [y_h, torch.empty_like(y_h).pin_memory()]
-        ev_in = [torch.cuda.Event(), torch.cuda.Event()]
-        ev_comp = [torch.cuda.Event(), torch.cuda.Event()]
-        ev_out = [torch.cuda.Event(), torch.cuda.Event()]
-        ev_fork = torch.cuda.Event()
-
-        def steps_graph(n):
-            ev_fork.record(stream)                     # the side streams join the capture here
-            s_in.wait_event(ev_fork)
-            s_out.wait_event(ev_fork)
-            for i in range(n):
-                b = i % 2
-                if i >= 2:
-                    s_in.wait_event(ev_comp[b])        # step i-2's call has read these inputs
-                with torch.cuda.stream(s_in):
-                    a_b[b].copy_(a_h, non_blocking=True)
-                    sa_b[b].copy_(sa_h, non_blocking=True)
-                    ev_in[b].record(s_in)
-                stream.wait_event(ev_in[b])
-                if i >= 2:
-                    stream.wait_event(ev_out[b])       # step i-2's result has left out_b[b]
-                fb.gemm_a8w8_blockscale_bpreshuffle_asm(a_b[b], s0["b"], out_b[b], sa_b[b], s0["sb"], None,
-                                                        cfg["splitK"], cfg["kernelName"], True)
-                ev_comp[b].record(stream)
-                s_out.wait_event(ev_comp[b])
-                with torch.cuda.stream(s_out):
-                    y_hb[b].copy_(out_b[b], non_blocking=True)
-                    ev_out[b].record(s_out)
-            stream.wait_event(ev_out[(n - 1) % 2])    # join both side streams back
-            stream.wait_event(ev_in[(n - 1) % 2])
-
-        per_graph = min(steps, 64)
-        with torch.cuda.stream(stream):
-            steps_graph(2)                             # eager warm-up outside capture
-            torch.cuda.synchronize(dev)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                steps_graph(per_graph)
-            g.replay()                                 # warm replay
-            torch.cuda.synchronize(dev)
-            barrier(world)
-            reps = max(1, steps // per_graph)
-            start.record(stream)
-            for _ in range(reps):
-                g.replay()
-            end.record(stream)
-            end.synchronize()
-        g.reset()
-        steps = reps * per_graph
-    else:
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                one()
-            barrier(world)
-            start.record(stream)
-            for _ in range(steps):
-                one()
-            end.record(stream)
-            end.synchronize()
+    with torch.cuda.stream(stream):
+        steps_graph(nb)                            # eager warm-up outside capture (registers every output)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            steps_graph(per_graph)
+        g.replay()                                 # warm replay
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        reps = max(3, math.ceil(min(args.steps, args.e2e_steps) / per_graph))
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        end.record(stream)
+        end.synchronize()
+    g.reset()
+    steps = reps * per_graph
     ms = max_over_ranks(start.elapsed_time(end), world, dev)
-    from fack_b200 import data
+    us = ms * 1e3 / steps
     work = data.flops(wl.M, wl.N, wl.K) * (1 if sharder else world) * steps
     return {"value": round(work / (ms / 1e3) / 1e12, 4), "unit": "TFLOPS",
-            "h2d_bytes_per_step": a_h.numel() * a_h.element_size() + sa_h.numel() * 4,
-            "d2h_bytes_per_step": y_h.numel() * 2, "steps": steps, "us_per_step": round(ms * 1e3 / steps, 2),
-            "api": ("fack_b200.gemm_a8w8_blockscale_bpreshuffle_asm with the plan of get_config; per step: pinned "
-                    "copy-in, call, copy-out on three streams over two buffers, CUDA graphs of 64 steps"
-                    if pipelined else "fack_b200.dist.ShardedBlockscaleGemm; per step: copy-in, sharded call, "
-                    "copy-out on one stream")}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps, "us_per_step": round(us, 2),
+            "h2d_gbs": round(h2d / (us * 1e3), 2), "d2h_gbs": round(d2h / (us * 1e3), 2),
+            "api": ("fack_b200.dist.ShardedBlockscaleGemm (fused all-gather)" if sharder else
+                    "fack_b200.gemm_a8w8_blockscale_bpreshuffle_asm with the plan of get_config") +
+                   f"; per step: pinned copy-in, call, copy-out on three streams over {nb} output buffers, "
+                   f"{reps} CUDA graphs of {per_graph} steps"}
 
 
 # ------------------------------------------------------- reference arm --
@@ -581,7 +630,8 @@ def run_reference(args):
               f"matmul + bf16 (client/aiter/hsa/gfx942/driver.py:18-20 restated), torch CPU, {threads} threads")
     line = {"metric": METRIC, "value": round(value, 5), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantised e4m3)",
+            "scaling": "strong" if args.workload in SHARDED else "weak", "vs_baseline": None,
+            "dtype": "fp32 (dequantised e4m3)",
             "data": "synthetic (seeded; benchmark-config construction)", "impl": "reference",
             "config": {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "M": wl.M, "N": wl.N, "K": wl.K,
                        "parallelism": "host CPU, rank 0 only"},
@@ -598,12 +648,13 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="decode")
+    ap.add_argument("--workload", default="prefill")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="sharded workloads: peer stores from the GEMM epilogue, or NCCL all-gather + interleave")
     ap.add_argument("--rotate", type=int, default=0, help="input sets to rotate (0 = enough to exceed L2)")
-    ap.add_argument("--e2e-steps", type=int, default=500)
+    ap.add_argument("--e2e-steps", type=int, default=192, help="e2e steps (at least three CUDA graphs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the secondary decode-shape measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU oracle work for cpu_baseline")
     ap.add_argument("--ref-budget", type=float, default=90.0, help="seconds for the reference arm's steps")

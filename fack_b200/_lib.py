@@ -37,6 +37,11 @@ FACK_ERR_DEVICE_TIMEOUT = 8
 FACK_ERR_CUDA = 9
 FACK_ERR_SCRATCH_LIMIT = 10
 
+# Bytes of one rank's exchange state (fack_gemm_bs_allgather, fack_xchg_barrier).
+FACK_XCHG_BYTES = 128
+# Device status bits (fack_device_status).
+FACK_DEVICE_EXCHANGE = 32
+
 FACK_W_ROW_MAJOR = 0
 FACK_W_PACKED = 1
 
@@ -74,6 +79,10 @@ SIGNATURES = {
     "fack_gemm_bs_bcast": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
                                     ctypes.POINTER(_c_p), _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                     _c_p, _c_sz, _c_p]),
+    "fack_gemm_bs_allgather": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,
+                                        ctypes.POINTER(_c_p), _c_p, ctypes.POINTER(_c_p), _c_int, _c_int,
+                                        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_sz, _c_p]),
+    "fack_xchg_barrier": (_c_int, [_c_p, ctypes.POINTER(_c_p), _c_int, _c_int, _c_p]),
     "fack_ipc_get_handle": (_c_int, [_c_p, _c_p, _c_sz, ctypes.POINTER(_c_sz)]),
     "fack_ipc_open_handle": (_c_int, [_c_p, ctypes.POINTER(_c_p)]),
     "fack_ipc_close_handle": (_c_int, [_c_p]),

@@ -115,6 +115,21 @@ struct Cfg {
 };
 
 constexpr int kMaxPeers = 7;  // peer outputs of fack_gemm_bs_bcast (8 GPUs per node)
+constexpr int kMaxRanks = kMaxPeers + 1;
+constexpr unsigned int kStExchange = 32u;  // a peer's completion signal did not arrive in time
+
+// Completion state of the fused all-gather, one per rank in that rank's
+// device memory (FACK_XCHG_BYTES, zero before first use), mapped into every
+// other rank.  done[s] is written only by rank s (over NVLink): the number of
+// exchanges rank s has finished, i.e. after which every block rank s stores
+// into this rank's output has landed.
+struct XchgState {
+  unsigned int arrivals;              // CTAs of the current launch that have finished their stores
+  unsigned int reserved;
+  unsigned long long seq;             // exchanges this rank has taken part in
+  unsigned long long done[kMaxRanks];
+};
+static_assert(sizeof(XchgState) <= FACK_XCHG_BYTES, "exchange state outgrew FACK_XCHG_BYTES");
 
 struct Params {
   const float* x_scale;
@@ -126,12 +141,62 @@ struct Params {
   // every bf16 result is stored to out and to each peer_out[0..n_peer)
   __nv_bfloat16* peer_out[kMaxPeers];
   int n_peer;
+  // fused all-gather completion (NULL: none): this rank's state, and for each
+  // peer d the slot done[rank] of that peer's state (peer mapping)
+  XchgState* xchg;
+  unsigned long long* peer_done[kMaxPeers];
+  int rank, world;
   float* partials;             // [tiles][S][128][BN] fp32 for S > 1; NULL = reduce through DSMEM
   int M, N, K, KB;
   int split;
   int w_packed;
   uint64_t timeout_ns;
+  uint64_t xchg_timeout_ns;
 };
+
+// One exchange step of this rank: tell every peer that this rank's stores
+// into its output have landed (release store of the new step number into
+// done[rank] of each peer's state), then wait until every peer has said the
+// same to this rank (acquire loads of this rank's done[]).  The wait is
+// bounded: on expiry it ORs kStExchange into the status word and returns.
+// One thread; every call on a rank's state comes from one stream, in the same
+// order on every rank, so the step numbers agree.
+__device__ __noinline__ void xchg_signal_and_wait(XchgState* x, unsigned long long* const* peer_done, int n_peer,
+                                                  int rank, int world, uint64_t timeout_ns, unsigned int* status) {
+  const unsigned long long seq = x->seq + 1;
+  x->seq = seq;
+  for (int d = 0; d < n_peer; ++d) st_release_sys_u64(peer_done[d], seq);
+  const uint64_t t0 = global_timer_ns();
+  for (int s = 0; s < world; ++s) {
+    if (s == rank) continue;
+    while (ld_acquire_sys_u64(&x->done[s]) < seq) {
+      if (global_timer_ns() - t0 > timeout_ns) {
+        atomicOr(status, kStExchange);
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+// End of a GEMM launch with peer stores (all threads of each CTA): every
+// thread's stores are made visible system-wide, the CTA counts itself in, and
+// the last CTA of the grid runs the exchange step (the classic last-block
+// pattern: fence, then an atomic ticket).  The grid therefore completes only
+// once every rank's blocks have landed in this rank's output, so no separate
+// barrier or collective is needed on the stream.
+__device__ __forceinline__ void xchg_complete(const Params& p, unsigned int* status) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(&p.xchg->arrivals, 1u) == total - 1) {
+      __threadfence_system();
+      p.xchg->arrivals = 0;  // every CTA of this launch has counted itself: ready for the next launch
+      xchg_signal_and_wait(p.xchg, p.peer_done, p.n_peer, p.rank, p.world, p.xchg_timeout_ns, status);
+    }
+  }
+}
 
 __device__ __forceinline__ uint2 pack_bf16x4(const float4& v) {
   __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
@@ -616,56 +681,62 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       tmem_dealloc(tmem_base, C::kTmemCols);
   }
 
-  if (S == 1) {
-    if (!ok || rows <= 0) return;
-    // 16-byte vectors of the staged bf16 tile along rows of Y
-    const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffA);
-    constexpr int kRowChunks = BN / 8;
-    for (int c = threadIdx.x; c < rows * kRowChunks; c += kThreads) {
-      const int r = c / kRowChunks, cc = c % kRowChunks;
-      const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
-      store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
+  // Output stores; every path returns here so that, with the fused
+  // all-gather, every CTA reaches the completion step below.
+  auto store_output = [&]() {
+    if (S == 1) {
+      if (!ok || rows <= 0) return;
+      // 16-byte vectors of the staged bf16 tile along rows of Y
+      const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffA);
+      constexpr int kRowChunks = BN / 8;
+      for (int c = threadIdx.x; c < rows * kRowChunks; c += kThreads) {
+        const int r = c / kRowChunks, cc = c % kRowChunks;
+        const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
+        store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
+      }
+      if (p.n_peer) __threadfence_system();  // peer stores are visible before this grid completes
+      return;
     }
-    if (p.n_peer) __threadfence_system();  // peer stores are visible before this grid completes
-    return;
-  }
 
-  // Split-K.  Every CTA of the cluster arrives at every cluster barrier, also
-  // after an abort, so none waits forever; each then sums a disjoint block of
-  // rows over the slices in fixed order 0..S-1 (bitwise reproducible).
-  const int rows_v = rows > 0 ? rows : 0;
-  const int per = (rows_v + S - 1) / S;
-  const int r0 = s * per;
-  const int r1 = min(rows_v, r0 + per);
-  const int rank_step = PAIR ? 2 : 1;               // cluster rank of slice t: (mt & 1) + rank_step * t
-  const int rank0 = PAIR ? static_cast<int>(mt & 1) : 0;
-  if (p.partials == nullptr) {
-    // Partials stay in each CTA's shared staging tile; peers read them over
-    // distributed shared memory.  The second barrier keeps every CTA (and so
-    // its shared memory) alive until all peers have finished reading.
+    // Split-K.  Every CTA of the cluster arrives at every cluster barrier, also
+    // after an abort, so none waits forever; each then sums a disjoint block of
+    // rows over the slices in fixed order 0..S-1 (bitwise reproducible).
+    const int rows_v = rows > 0 ? rows : 0;
+    const int per = (rows_v + S - 1) / S;
+    const int r0 = s * per;
+    const int r1 = min(rows_v, r0 + per);
+    const int rank_step = PAIR ? 2 : 1;               // cluster rank of slice t: (mt & 1) + rank_step * t
+    const int rank0 = PAIR ? static_cast<int>(mt & 1) : 0;
+    if (p.partials == nullptr) {
+      // Partials stay in each CTA's shared staging tile; peers read them over
+      // distributed shared memory.  The second barrier keeps every CTA (and so
+      // its shared memory) alive until all peers have finished reading.
+      cluster_sync_all();
+      if (ok)
+        reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1, p,
+                                      static_cast<int64_t>(m0) * p.ldo + n0);
+      if (p.n_peer) __threadfence_system();
+      cluster_sync_all();
+      return;
+    }
+    // Caller-provided workspace (reduce-scatter through L2): each slice writes
+    // the rows the other slices reduce, the cluster barrier publishes them, and
+    // each slice sums its own rows from the workspace and its own staging.  No
+    // CTA reads another's shared memory, so there is no second barrier.
+    const int64_t tile = static_cast<int64_t>(mt) * (p.N / BN) + nt;
+    const float* stg32 = reinterpret_cast<const float*>(smem + C::kOffA);
+    if (ok) {
+      copy_partial<BN, C::kPitch32>(stg32, rows_v, r0, r1, p.partials + (tile * S + s) * kTileM * BN);
+      __threadfence();
+    }
     cluster_sync_all();
-    if (ok)
-      reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1, p,
-                                    static_cast<int64_t>(m0) * p.ldo + n0);
+    if (!ok) return;
+    reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1, p,
+                                   static_cast<int64_t>(m0) * p.ldo + n0);
     if (p.n_peer) __threadfence_system();
-    cluster_sync_all();
-    return;
-  }
-  // Caller-provided workspace (reduce-scatter through L2): each slice writes
-  // the rows the other slices reduce, the cluster barrier publishes them, and
-  // each slice sums its own rows from the workspace and its own staging.  No
-  // CTA reads another's shared memory, so there is no second barrier.
-  const int64_t tile = static_cast<int64_t>(mt) * (p.N / BN) + nt;
-  const float* stg32 = reinterpret_cast<const float*>(smem + C::kOffA);
-  if (ok) {
-    copy_partial<BN, C::kPitch32>(stg32, rows_v, r0, r1, p.partials + (tile * S + s) * kTileM * BN);
-    __threadfence();
-  }
-  cluster_sync_all();
-  if (!ok) return;
-  reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1, p,
-                                 static_cast<int64_t>(m0) * p.ldo + n0);
-  if (p.n_peer) __threadfence_system();
+  };
+  store_output();
+  if (p.xchg) xchg_complete(p, status);
 }
 
 // ------------------------------------------------------ small-M (swapped) --
@@ -888,38 +959,47 @@ gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   const int items = M * 32;                        // 4-column chunks of the M x 128 output block
   const float* stg = reinterpret_cast<const float*>(smem + C::kOffW);
   if (S == 1) {
-    if (!ok) return;
-    for (int it = threadIdx.x; it < items; it += C::kThreads) {
-      const int t = it >> 5, c = (it & 31) * 4;
-      const float4 v = *reinterpret_cast<const float4*>(stg + t * C::kPitch + c);
-      store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(v));
-    }
-    if (p.n_peer) __threadfence_system();
-    return;
-  }
-  // split-K: every CTA of the cluster reaches both barriers, also after an
-  // abort; each sums a disjoint range of the block's chunks over the slices in
-  // order 0..S-1 (bitwise reproducible)
-  cluster_sync_all();
-  if (ok) {
-    const int i0 = (s * items) / S, i1 = ((s + 1) * items) / S;
-    const uint32_t sbase = base + C::kOffW;
-    for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += C::kThreads) {
-      const int t = it >> 5, c = (it & 31) * 4;
-      const uint32_t addr = sbase + static_cast<uint32_t>((t * C::kPitch + c) * 4);
-      float4 sum = dsmem_ld4(dsmem_map(addr, 0));
-      for (int r = 1; r < S; ++r) {
-        const float4 v = dsmem_ld4(dsmem_map(addr, r));
-        sum.x += v.x;
-        sum.y += v.y;
-        sum.z += v.z;
-        sum.w += v.w;
+    if (ok) {
+      for (int it = threadIdx.x; it < items; it += C::kThreads) {
+        const int t = it >> 5, c = (it & 31) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(stg + t * C::kPitch + c);
+        store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(v));
       }
-      store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(sum));
+      if (p.n_peer) __threadfence_system();
     }
-    if (p.n_peer) __threadfence_system();
+  } else {
+    // split-K: every CTA of the cluster reaches both barriers, also after an
+    // abort; each sums a disjoint range of the block's chunks over the slices in
+    // order 0..S-1 (bitwise reproducible)
+    cluster_sync_all();
+    if (ok) {
+      const int i0 = (s * items) / S, i1 = ((s + 1) * items) / S;
+      const uint32_t sbase = base + C::kOffW;
+      for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += C::kThreads) {
+        const int t = it >> 5, c = (it & 31) * 4;
+        const uint32_t addr = sbase + static_cast<uint32_t>((t * C::kPitch + c) * 4);
+        float4 sum = dsmem_ld4(dsmem_map(addr, 0));
+        for (int r = 1; r < S; ++r) {
+          const float4 v = dsmem_ld4(dsmem_map(addr, r));
+          sum.x += v.x;
+          sum.y += v.y;
+          sum.z += v.z;
+          sum.w += v.w;
+        }
+        store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(sum));
+      }
+      if (p.n_peer) __threadfence_system();
+    }
+    cluster_sync_all();
   }
-  cluster_sync_all();
+  if (p.xchg) xchg_complete(p, status);
+}
+
+// A stand-alone exchange step (one thread): orders a rank's next peer stores
+// after everything its stream did before, on every rank.
+__global__ void xchg_barrier_kernel(XchgState* x, Params pd, uint64_t timeout_ns) {
+  if (threadIdx.x == 0)
+    xchg_signal_and_wait(x, pd.peer_done, pd.n_peer, pd.rank, pd.world, timeout_ns, &g_status);
 }
 
 // ------------------------------------------------------------------ prepack --
@@ -1460,10 +1540,14 @@ int fack_gemm_bs_prepack_w(const void* wq, int64_t ldw, const float* w_scale, in
 
 // fack_gemm_bs_ex with the result also stored to n_peers peer copies of the
 // output block (same ldo); n_peers = 0 is fack_gemm_bs_ex.
+// With `xchg` (the fused all-gather: world - 1 peers, this rank's exchange
+// state and each peer's mapped state, in rank order without `rank`) the
+// launch also runs the completion step of xchg_complete.
 static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
                         int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
                         void* const* peer_outs, int n_peers, int M, int N, int K, int tile_m, int tile_n,
-                        int split_k, void* workspace, size_t workspace_bytes, void* stream) {
+                        int split_k, void* workspace, size_t workspace_bytes, void* stream, void* xchg = nullptr,
+                        void* const* peer_xchg = nullptr, int rank = 0, int world = 1) {
   if (M < 1 || N < kBlk || K < kBlk || N % kBlk || K % kBlk) return FACK_ERR_BAD_SHAPE;
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peer_outs)) return FACK_ERR_BAD_ARG;
   for (int i = 0; i < n_peers; ++i)
@@ -1517,9 +1601,31 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   p.split = sp;
   p.w_packed = wq_packed;
   p.timeout_ns = 2000000000ull;  // 2 s: far above any legitimate wait, short enough to report a lost arrival
+  p.xchg = static_cast<XchgState*>(xchg);
+  p.rank = rank;
+  p.world = world;
+  for (int i = 0; i < kMaxPeers; ++i) p.peer_done[i] = nullptr;
+  if (xchg) {
+    for (int i = 0; i < n_peers; ++i)
+      p.peer_done[i] = reinterpret_cast<unsigned long long*>(static_cast<char*>(peer_xchg[i]) +
+                                                             offsetof(XchgState, done)) + rank;
+  }
+  // a peer may legitimately start its step later than this rank (host-side
+  // work between steps); 10 s bounds the wait for one that never comes
+  p.xchg_timeout_ns = 10000000000ull;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return launch(d, tm, bn, tw, tx, p, M, s);
+}
+
+// Rules shared by the entry points of the fused all-gather.
+static int check_exchange(void* xchg, void* const* peer_xchg, int rank, int world) {
+  if (world < 2 || world > kMaxRanks || rank < 0 || rank >= world) return FACK_ERR_BAD_ARG;
+  if (!peer_xchg) return FACK_ERR_BAD_ARG;
+  if (!xchg || !aligned(xchg, 16)) return FACK_ERR_BAD_ALIGN;
+  for (int i = 0; i < world - 1; ++i)
+    if (!peer_xchg[i] || !aligned(peer_xchg[i], 16)) return FACK_ERR_BAD_ALIGN;
+  return FACK_OK;
 }
 
 extern "C" {
@@ -1538,6 +1644,39 @@ int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packe
                        void* workspace, size_t workspace_bytes, void* stream) {
   return gemm_bs_impl(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, peer_outs,
                       n_peers, M, N, K, tile_m, tile_n, split_k, workspace, workspace_bytes, stream);
+}
+
+int fack_gemm_bs_allgather(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                           int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                           void* const* peer_outs, void* xchg, void* const* peer_xchg, int rank, int world, int M,
+                           int N, int K, int tile_m, int tile_n, int split_k, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  const int st = check_exchange(xchg, peer_xchg, rank, world);
+  if (st != FACK_OK) return st;
+  if (!peer_outs) return FACK_ERR_BAD_ARG;
+  return gemm_bs_impl(xq, ldx, wq, wq_packed, x_scale, xs_stride_m, xs_stride_kb, w_scale, out, ldo, peer_outs,
+                      world - 1, M, N, K, tile_m, tile_n, split_k, workspace, workspace_bytes, stream, xchg,
+                      peer_xchg, rank, world);
+}
+
+int fack_xchg_barrier(void* xchg, void* const* peer_xchg, int rank, int world, void* stream) {
+  const int st0 = check_exchange(xchg, peer_xchg, rank, world);
+  if (st0 != FACK_OK) return st0;
+  DeviceInfo* d = nullptr;
+  const int st = device_info(&d);
+  if (st != FACK_OK) return st;
+  Params pd;
+  memset(&pd, 0, sizeof(pd));
+  pd.n_peer = world - 1;
+  pd.rank = rank;
+  pd.world = world;
+  for (int i = 0; i < world - 1; ++i)
+    pd.peer_done[i] = reinterpret_cast<unsigned long long*>(static_cast<char*>(peer_xchg[i]) +
+                                                            offsetof(XchgState, done)) + rank;
+  xchg_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<XchgState*>(xchg), pd,
+                                                                        10000000000ull);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? FACK_OK : fail(FACK_ERR_LAUNCH, "xchg_barrier_kernel", e);
 }
 
 // ------------------------------------------------------------ CUDA IPC --

@@ -462,6 +462,19 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// ------------------------------------------------- cross-GPU signalling --
+// A store that publishes everything this thread observed before it (release)
+// at system scope, so another GPU reading the value with an acquire load sees
+// those writes too; used on peer-mapped memory over NVLink.
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // --------------------------------------------------------------- clusters --
 // barrier.cluster.*.aligned: every lane of the warp must execute it together,
 // so reconverge first (callers reach it after per-lane loops).

@@ -8,10 +8,12 @@ computes its [M, N/g] block with the single-GPU kernel.  Two ways to assemble
 the replicated row-major Y[M, N]:
 
 * ``mode="fused"`` (GPUs): the GEMM's own epilogue stores each bf16 tile into
-  column block r of every rank's Y through NVLink peer mappings (CUDA IPC;
-  ``fack_gemm_bs_bcast``), so the exchange overlaps the math tile by tile and
-  no separate gather or interleave runs; a one-element all-reduce before and
-  after the launch, on the same stream, orders it against the other ranks.
+  column block r of every rank's Y through NVLink peer mappings (CUDA IPC),
+  so the exchange overlaps the math tile by tile and no separate gather or
+  interleave runs.  The launch orders itself against the other ranks on the
+  device (``fack_gemm_bs_allgather``): its last CTA signals every peer over
+  NVLink and waits, bounded, for every peer's signal, so the call holds no
+  collective and its completion on the stream means Y is whole.
 * ``mode="nccl"``: the block goes to this rank's slot of a [g, M, N/g] gather
   buffer, an in-place NCCL all-gather fills the other slots, and a
   column-interleave kernel assembles Y (also the gloo path of the CPU tests).
@@ -21,12 +23,26 @@ shard is made of whole 128x128 weight-scale blocks.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
 BLOCK = 128
+XCHG_BYTES = 128  # FACK_XCHG_BYTES: one rank's exchange state
+
+
+@dataclass
+class ExchangeState:
+    """One rank's exchange state of the fused all-gather: ``ptr`` is this
+    rank's FACK_XCHG_BYTES in its own device memory (held by ``tensor``),
+    ``peer_ptrs`` every other rank's state mapped here, in rank order."""
+    rank: int
+    world: int
+    ptr: int
+    peer_ptrs: list
+    tensor: torch.Tensor
 
 
 def shard_bounds(N: int, world: int, rank: int):
@@ -55,9 +71,14 @@ def _default_interleave(gathered, out):
     return gather_interleave(gathered, out)
 
 
-def _default_local_gemm_peers(xq, wq, x_scale, w_scale, out, peer_addrs):
+def _default_local_gemm_peers(xq, wq, x_scale, w_scale, out, peer_addrs, xchg):
     from .ops import gemm_blockscale
-    return gemm_blockscale(xq, wq, x_scale, w_scale, out=out, peer_outs=peer_addrs)
+    return gemm_blockscale(xq, wq, x_scale, w_scale, out=out, peer_outs=peer_addrs, xchg=xchg)
+
+
+def _default_xchg_barrier(xchg):
+    from .ops import xchg_barrier
+    xchg_barrier(xchg, xchg.tensor.device)
 
 
 class CudaIpc:
@@ -139,15 +160,25 @@ class ShardedBlockscaleGemm:
     ``mode="nccl"``: ``local_gemm(xq, wq_shard, x_scale, ws_shard, out)`` and
     ``interleave(gathered, out)`` default to this library's CUDA kernels; the
     CPU tests substitute checkers to exercise the sharding and gather logic
-    on gloo ranks.  ``mode="fused"``: ``out`` (row-major [M, N], required)
-    is registered with every rank on first use (a collective: all ranks pass
-    their buffers in the same order, outside CUDA-graph capture), then each
-    call is barrier -> GEMM storing to every rank's ``out`` -> barrier.
+    on gloo ranks.
+
+    ``mode="fused"``: ``out`` (row-major [M, N], required) is registered with
+    every rank on first use, and so is the exchange state on the first call
+    (collectives: all ranks make the same calls in the same order, outside
+    CUDA-graph capture).  Each call is one launch,
+    ``local_gemm_peers(xq, wq_shard, x_scale, ws_shard, out_block, peer_addrs,
+    xchg)``, which stores this rank's block into every rank's ``out`` and
+    returns on the stream only once every rank's block has landed here.  A
+    peer may store into ``out`` as soon as every rank has finished the
+    previous call, so a call whose ``out`` is the previous call's ``out``
+    first runs ``xchg_barrier(xchg)`` (one more exchange step: no rank writes
+    before every rank's earlier work on its stream is complete).  Alternating
+    between two registered outputs needs no such step.
     """
 
     def __init__(self, group=None, local_gemm: Optional[Callable] = None,
                  interleave: Optional[Callable] = None, mode: str = "nccl", ipc=None,
-                 local_gemm_peers: Optional[Callable] = None):
+                 local_gemm_peers: Optional[Callable] = None, xchg_barrier: Optional[Callable] = None):
         if mode not in ("nccl", "fused"):
             raise ValueError("mode must be 'nccl' or 'fused'")
         self.group = group
@@ -156,6 +187,7 @@ class ShardedBlockscaleGemm:
         self.mode = mode
         self.local_gemm = local_gemm or _default_local_gemm
         self.local_gemm_peers = local_gemm_peers or _default_local_gemm_peers
+        self.xchg_barrier = xchg_barrier or _default_xchg_barrier
         self.interleave = interleave or _default_interleave
         self.ipc = ipc
         self._gather = None
@@ -165,7 +197,9 @@ class ShardedBlockscaleGemm:
         # store into it; close() lets go.
         self._peers: dict = {}
         self._mapped: list = []    # mapped peer bases, released by close()
-        self._flag = None
+        self._xchg: Optional[ExchangeState] = None
+        self._last_out = None      # key of the previous fused call's out
+        self.barriers = 0          # exchange steps run on their own (same out twice in a row)
 
     def gather_buffer(self, M: int, ns: int, device) -> torch.Tensor:
         g = self._gather
@@ -189,17 +223,30 @@ class ShardedBlockscaleGemm:
             self._peers[key] = (out, [addr for _, addr in pairs])
         return self._peers[key][1]
 
-    def _barrier(self, device) -> None:
-        if self._flag is None or self._flag.device != torch.device(device):
-            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
-        dist.all_reduce(self._flag, group=self.group)
+    def exchange_state(self, device) -> ExchangeState:
+        """This rank's exchange state, created and mapped by every rank on
+        first use (a collective, outside CUDA-graph capture)."""
+        x = self._xchg
+        if x is None or x.tensor.device != torch.device(device):
+            if x is not None:
+                raise RuntimeError("the exchange state lives on one device; use one sharder per device")
+            if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("create the exchange state before CUDA-graph capture (call once eagerly)")
+            if self.ipc is None:
+                self.ipc = CudaIpc()
+            t = torch.zeros(XCHG_BYTES // 8, dtype=torch.int64, device=device)
+            pairs = exchange_peer_addresses(t, self.ipc, self.group)
+            self._mapped += [base for base, _ in pairs]
+            x = ExchangeState(self.rank, self.world, t.data_ptr(), [addr for _, addr in pairs], t)
+            self._xchg = x
+        return x
 
     def close(self) -> None:
-        """Release the peer mappings and the registered outputs (before the
-        process group is destroyed)."""
+        """Release the peer mappings, the registered outputs and the exchange
+        state (before the process group is destroyed)."""
         for base in self._mapped:
             self.ipc.close(base)
-        self._mapped, self._peers = [], {}
+        self._mapped, self._peers, self._xchg, self._last_out = [], {}, None, None
 
     def __call__(self, xq, wq_shard, x_scale, ws_shard, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         M = xq.shape[0]
@@ -210,12 +257,16 @@ class ShardedBlockscaleGemm:
             if out is None or tuple(out.shape) != (M, self.world * ns) or not out.is_contiguous():
                 raise ValueError(f"fused mode needs a contiguous out of shape [{M}, {self.world * ns}]")
             peers = self.register(out)
+            xchg = self.exchange_state(out.device)
             col = self.rank * ns
             nbytes = out.element_size() * col                 # byte offset of this rank's column block
-            self._barrier(out.device)                         # no rank still reads the Y about to be written
+            key = (out.data_ptr(), out.numel())
+            if key == self._last_out:                         # a peer could overwrite what this rank still reads
+                self.xchg_barrier(xchg)
+                self.barriers += 1
             self.local_gemm_peers(xq, wq_shard, x_scale, ws_shard, out[:, col:col + ns],
-                                  [a + nbytes for a in peers])
-            self._barrier(out.device)                         # every rank's blocks have landed everywhere
+                                  [a + nbytes for a in peers], xchg)
+            self._last_out = key
             return out
         gathered = self.gather_buffer(M, ns, xq.device)
         mine = gathered[self.rank]

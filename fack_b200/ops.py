@@ -164,12 +164,16 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
 
 
 def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m=0, tile_n=0,
-            reduce="dsmem", peer_outs=()):
+            reduce="dsmem", peer_outs=(), xchg=None):
     """reduce = "dsmem": split-K slices combine through the cluster's shared
     memory (no workspace, nothing allocated); "global": through a cached
     workspace in global memory.  ``peer_outs``: device addresses (this
     process's mappings of other GPUs' memory) of more copies of ``out``'s
-    block, same row stride; every result is stored to each of them too."""
+    block, same row stride; every result is stored to each of them too.
+    ``xchg`` (with ``peer_outs`` for every other rank, in rank order): the
+    exchange state of the fused all-gather (attributes ``rank``, ``world``,
+    ``ptr`` and ``peer_ptrs``); the launch then completes only once every
+    rank's block has landed in this rank's output (fack_gemm_bs_allgather)."""
     M, K = xq.shape
     N = wq.shape[0]
     dev = xq.device
@@ -180,25 +184,50 @@ def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m
         args = (xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
                 x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0))
         tail = (M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
-        if peer_outs:
+        if xchg is not None:
+            if len(peer_outs) != xchg.world - 1 or len(xchg.peer_ptrs) != xchg.world - 1:
+                raise ValueError("the fused all-gather needs one peer output and one peer state per other rank")
+            peers = (ctypes.c_void_p * len(peer_outs))(*[int(a) for a in peer_outs])
+            pstates = (ctypes.c_void_p * len(xchg.peer_ptrs))(*[int(a) for a in xchg.peer_ptrs])
+            st = lib.fack_gemm_bs_allgather(*args, peers, int(xchg.ptr), pstates, int(xchg.rank), int(xchg.world),
+                                            *tail)
+            what = "fack_gemm_bs_allgather"
+        elif peer_outs:
             peers = (ctypes.c_void_p * len(peer_outs))(*[int(a) for a in peer_outs])
             st = lib.fack_gemm_bs_bcast(*args, peers, len(peer_outs), *tail)
+            what = "fack_gemm_bs_bcast"
         else:
             st = lib.fack_gemm_bs_ex(*args, *tail)
-    _lib.check(st, "fack_gemm_bs_bcast" if peer_outs else "fack_gemm_bs_ex")
+            what = "fack_gemm_bs_ex"
+    _lib.check(st, what)
     return out
+
+
+def xchg_barrier(xchg, device) -> None:
+    """One exchange step alone on the current stream of ``device``
+    (fack_xchg_barrier): no rank's next fused all-gather stores into an output
+    before every rank's work queued before this point is complete."""
+    lib = _lib.load()
+    dev = torch.device(device)
+    pstates = (ctypes.c_void_p * len(xchg.peer_ptrs))(*[int(a) for a in xchg.peer_ptrs])
+    with torch.cuda.device(dev):
+        st = lib.fack_xchg_barrier(int(xchg.ptr), pstates, int(xchg.rank), int(xchg.world), _stream_handle(dev))
+    _lib.check(st, "fack_xchg_barrier")
 
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                     out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0, tile_m: int = 0,
-                    reduce: str = "dsmem", peer_outs=()) -> torch.Tensor:
+                    reduce: str = "dsmem", peer_outs=(), xchg=None) -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
     :func:`shuffle_weight` (detected by its ``is_shuffled`` mark).
     ``peer_outs`` (up to 7 device addresses of peer mappings, each the same
     block as ``out`` in another GPU's output, same row stride) makes the
-    kernel store every result there too (``fack_gemm_bs_bcast``).
+    kernel store every result there too (``fack_gemm_bs_bcast``); with
+    ``xchg`` as well (one peer output per other rank, the exchange state of
+    :class:`fack_b200.dist.ExchangeState`) the launch also waits, on the
+    device, until every rank's block has landed (``fack_gemm_bs_allgather``).
     """
     if len(peer_outs) > 7:
         raise ValueError("at most 7 peer outputs")
@@ -219,7 +248,7 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
     if reduce not in ("dsmem", "global"):
         raise ValueError("reduce must be 'dsmem' or 'global'")
     return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_m,
-                   tile_n, reduce, tuple(peer_outs))
+                   tile_n, reduce, tuple(peer_outs), xchg)
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):

@@ -21,7 +21,11 @@
  *   - no entry point allocates, frees or synchronises, so every launch can be
  *     captured in a CUDA graph (the caller sizes and owns the workspace);
  *   - the device must be sm_100 (B200); other devices return
- *     FACK_ERR_UNSUPPORTED_ARCH.
+ *     FACK_ERR_UNSUPPORTED_ARCH;
+ *   - the calling thread's current device (cudaGetDevice) must be the device
+ *     that owns `stream` and the operands: per-device state (the plan's
+ *     occupancy queries, the no-allocation scratch, the status word) is
+ *     looked up for the current device, not derived from `stream`.
  */
 #ifndef FACK_GEMM_H
 #define FACK_GEMM_H
@@ -141,6 +145,59 @@ int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packe
                        int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
                        void* const* peer_outs, int n_peers, int M, int N, int K, int tile_m, int tile_n, int split_k,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Bytes of one rank's exchange state for fack_gemm_bs_allgather and
+ * fack_xchg_barrier: device memory, 16-byte aligned, zero before its first
+ * use, mapped into every other rank like the outputs (fack_ipc_*).
+ */
+#define FACK_XCHG_BYTES 128
+
+/*
+ * The fused compute + all-gather with its own completion: fack_gemm_bs_bcast
+ * to the world - 1 peers (peer_outs, in rank order without `rank`), where the
+ * last CTA of the grid to finish then signals every peer that this rank's
+ * blocks have landed (a release store over NVLink into that peer's exchange
+ * state, peer_xchg[i] in the same order) and waits, bounded by 10 s, until
+ * every peer has signalled this rank.  When the launch completes on `stream`,
+ * this rank's Y holds every rank's block: no barrier or collective is needed
+ * around it.  2 <= world <= 8.  On a wait that runs out the device status word
+ * gets FACK_DEVICE_EXCHANGE (fack_device_status) and the launch still ends.
+ *
+ * Ordering contract: every rank makes the same sequence of allgather and
+ * barrier calls on one stream with its exchange state.  A peer may store into
+ * this rank's output as soon as every rank has completed the previous
+ * exchange, so an output buffer must not be passed to two consecutive calls
+ * while work that reads it may still be queued behind the first one; either
+ * alternate between two registered outputs (work queued on `stream` before a
+ * call is complete before any peer stores into the buffer of the call after
+ * it) or put fack_xchg_barrier before the second call.
+ * No counterpart in the reference (one GPU per process, no collective:
+ * client/aiter/docs/validation.md:42-46).
+ */
+int fack_gemm_bs_allgather(const void* xq, int64_t ldx, const void* wq, int wq_packed, const float* x_scale,
+                           int64_t xs_stride_m, int64_t xs_stride_kb, const float* w_scale, void* out, int64_t ldo,
+                           void* const* peer_outs, void* xchg, void* const* peer_xchg, int rank, int world,
+                           int M, int N, int K, int tile_m, int tile_n, int split_k,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One exchange step alone (a one-thread kernel on `stream`): signals every
+ * peer, then waits (bounded by 10 s) until every peer has signalled, so that
+ * no rank's next fack_gemm_bs_allgather stores into an output before every
+ * rank's earlier work on its stream is complete.  Same arguments and
+ * ordering contract as fack_gemm_bs_allgather.
+ */
+int fack_xchg_barrier(void* xchg, void* const* peer_xchg, int rank, int world, void* stream);
+
+/* Device status bits (fack_device_status). */
+#define FACK_DEVICE_PRODUCER 1u   /* a TMA producer's wait for a free stage ran out */
+#define FACK_DEVICE_MMA 2u        /* the MMA issuer's wait ran out */
+#define FACK_DEVICE_EPILOGUE 8u   /* a rescale / epilogue warp's wait ran out */
+#define FACK_DEVICE_DRAIN 16u     /* draining in-flight copies or MMAs ran out */
+#define FACK_DEVICE_EXCHANGE 32u  /* a peer's exchange signal did not arrive */
+#define FACK_DEVICE_QUANT 64u     /* a wait in the activation quantiser ran out */
+#define FACK_DEVICE_TN 128u       /* a wait in the sibling GEMM (fack_gemm_tn) ran out */
 
 /*
  * CUDA IPC for the peer outputs.  fack_ipc_get_handle: the IPC handle (64
@@ -295,7 +352,9 @@ int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
  * two streams without an ordering between them) race and corrupt each other;
  * order them on one stream.  The first call on each device looks up the
  * buffer's device address (a runtime query, no allocation): make that first
- * call before any stream capture.  It calls no cudaMalloc or cudaFree.
+ * call before any stream capture.  The buffer used is the current device's
+ * (cudaGetDevice), so make the device that owns `stream` current before the
+ * call.  It calls no cudaMalloc or cudaFree.
  */
 int fack_gemm_bs_noalloc(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                          const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,

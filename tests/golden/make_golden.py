@@ -25,6 +25,7 @@ from __future__ import annotations
 import hashlib
 import importlib.util
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -34,7 +35,6 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REF = Path("/root/reference")
 SYMBOL = "_ZN5aiter42fp8gemm_bf16_blockscale_BpreShuffle_32x128E"
 
 # (name, m, n, k, seed): shapes the reference itself uses, plus edge cases.
@@ -100,7 +100,7 @@ def run_reference_prepare(ref_root: Path, m: int, n: int, k: int, seed: int):
     return case, hashlib.sha256(driver_path.read_bytes()).hexdigest()
 
 
-def main(ref_root: Path = DEFAULT_REF) -> None:
+def main(ref_root: Path) -> None:
     index = {}
     for name, m, n, k, seed in CASES:
         case, sha = run_reference_prepare(ref_root, m, n, k, seed)
@@ -118,4 +118,8 @@ def main(ref_root: Path = DEFAULT_REF) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF)
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FACK_REFERENCE_ROOT")
+    if not root:
+        sys.exit(f"usage: python {Path(__file__).name} REFERENCE_ROOT  (or set FACK_REFERENCE_ROOT): "
+                 "the reference checkout whose driver generates the vectors")
+    main(Path(root))

@@ -24,6 +24,7 @@ from __future__ import annotations
 import hashlib
 import importlib.util
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -32,7 +33,6 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REF = Path("/root/reference")
 SYMBOLS = {"bf16": "golden_bf16gemm_fp32bf16_tn", "i8": "golden_I8gemm_bf16_perTokenI8_BpreShuffle_tn"}
 
 # (name, family, m, n, k, bpreshuffle, seed); N % 64 (bf16) / % 256 (int8), K % 128 (gemm_driver.py:41-42)
@@ -100,7 +100,7 @@ def run_reference_prepare(ref_root: Path, family, m, n, k, bpreshuffle, seed):
     return case, hashlib.sha256(path.read_bytes()).hexdigest()
 
 
-def main(ref_root: Path = DEFAULT_REF) -> None:
+def main(ref_root: Path) -> None:
     index = {}
     for name, family, m, n, k, shuffled, seed in CASES:
         case, sha = run_reference_prepare(ref_root, family, m, n, k, shuffled, seed)
@@ -122,4 +122,8 @@ def main(ref_root: Path = DEFAULT_REF) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF)
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FACK_REFERENCE_ROOT")
+    if not root:
+        sys.exit(f"usage: python {Path(__file__).name} REFERENCE_ROOT  (or set FACK_REFERENCE_ROOT): "
+                 "the reference checkout whose driver generates the vectors")
+    main(Path(root))

@@ -100,56 +100,76 @@ def test_shard_bounds_and_weight_slices():
 # mappings.  On CPU ranks the "GPU memory" of rank j is a shared-memory tensor
 # ys[j]; the fake IPC layer hands out addresses (j + 1) << 40 + byte offset, and
 # the fake GEMM resolves them, so the test checks the handle exchange, the
-# offset arithmetic and the barrier order of the real ShardedBlockscaleGemm.
+# offset arithmetic and when the real ShardedBlockscaleGemm adds an exchange
+# step of its own.  On the GPU the launch's last CTA signals the peers and
+# waits for theirs; here a gloo barrier after the stores stands in for it.
 
 class _FakeIpc:
+    """Handles name (rank, buffer id); rank j's buffer b maps to
+    ((j + 1) << 40) | (b << 32), the tensor starting at the mapping's base.
+    ``ids`` gives the buffer id of a tensor by data_ptr (default 0)."""
     HANDLE_BYTES = 64
 
-    def __init__(self, rank):
+    def __init__(self, rank, ids=None):
         self.rank = rank
+        self.ids = ids or {}
         self.opened, self.closed = [], []
 
     def handle(self, t):
-        return bytes([self.rank]) + bytes(63), 0   # this rank's Y starts at its mapping's base
+        return bytes([self.rank, self.ids.get(t.data_ptr(), 0)]) + bytes(62), 0
 
     def open(self, handle):
         j = handle[0]
         self.opened.append(j)
-        return (j + 1) << 40
+        return ((j + 1) << 40) | (handle[1] << 32)
 
     def close(self, base):
         self.closed.append(base)
 
 
-def _fused_worker(rank, world, port, M, N, K, ys):
+def _fused_worker(rank, world, port, M, N, K, ys, alt):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from fack_b200 import data
-        from fack_b200.dist import ShardedBlockscaleGemm, shard_weight
+        from fack_b200.dist import XCHG_BYTES, ShardedBlockscaleGemm, shard_weight
         from oracle.blockscale import reference_gemm
         xq, xs, wq, ws = data.make_inputs(data.Workload("dist", M, N, K), seed=4)
         wq_r, ws_r = shard_weight(wq, ws, rank, world)
+        calls = []
 
-        def local(xq_, wq_, xs_, ws_, out_view, peer_addrs):
+        def local(xq_, wq_, xs_, ws_, out_view, peer_addrs, xchg):
             block = reference_gemm(xq_, wq_, xs_, ws_)
             out_view.copy_(block)
-            assert len(peer_addrs) == world - 1
+            assert len(peer_addrs) == world - 1 and len(xchg.peer_ptrs) == world - 1
+            assert (xchg.rank, xchg.world) == (rank, world) and xchg.tensor.numel() * 8 == XCHG_BYTES
             for a in peer_addrs:
-                j = (a >> 40) - 1
+                j, bid = (a >> 40) - 1, (a >> 32) & 0xFF
                 assert j != rank and 0 <= j < world
-                col = (a & ((1 << 40) - 1)) // 2          # byte offset inside Y_j, row 0
-                ys[j][:, col:col + block.shape[1]].copy_(block)
+                col = (a & ((1 << 32) - 1)) // 2          # byte offset inside Y_j, row 0
+                (ys, alt)[bid][j][:, col:col + block.shape[1]].copy_(block)
+            calls.append("gemm")
+            dist.barrier()                                # the launch's own completion step
 
-        ipc = _FakeIpc(rank)
-        gemm = ShardedBlockscaleGemm(mode="fused", ipc=ipc, local_gemm_peers=local)
-        y = gemm(xq, wq_r, xs, ws_r, out=ys[rank])
-        assert y is ys[rank]
-        gemm(xq, wq_r, xs, ws_r, out=ys[rank])            # registered once: no second exchange
-        assert sorted(ipc.opened) == [j for j in range(world) if j != rank]
+        def barrier(xchg):
+            calls.append("barrier")
+            dist.barrier()
+
+        ipc = _FakeIpc(rank, ids={alt[rank].data_ptr(): 1})
+        gemm = ShardedBlockscaleGemm(mode="fused", ipc=ipc, local_gemm_peers=local, xchg_barrier=barrier)
+        outs = [ys[rank], alt[rank]]
+        y = gemm(xq, wq_r, xs, ws_r, out=outs[0])
+        assert y is outs[0]
+        gemm(xq, wq_r, xs, ws_r, out=outs[1])             # alternating outputs: no extra step
+        gemm(xq, wq_r, xs, ws_r, out=outs[0])
+        gemm(xq, wq_r, xs, ws_r, out=outs[0])             # the same output twice in a row: one extra step
+        assert calls == ["gemm", "gemm", "gemm", "barrier", "gemm"], calls
+        assert gemm.barriers == 1
+        # two outputs + the exchange state, each mapped from every peer once
+        assert sorted(ipc.opened) == sorted([j for j in range(world) if j != rank] * 3)
         gemm.close()
-        assert len(ipc.closed) == world - 1
+        assert len(ipc.closed) == 3 * (world - 1)
     finally:
         dist.destroy_process_group()
 
@@ -157,7 +177,8 @@ def _fused_worker(rank, world, port, M, N, K, ys):
 def test_fused_mode_two_gloo_ranks():
     world, M, N, K = 2, 33, 768, 384
     ys = [torch.full((M, N), float("nan"), dtype=torch.bfloat16).share_memory_() for _ in range(world)]
-    mp.start_processes(_fused_worker, args=(world, _free_port(), M, N, K, ys), nprocs=world,
+    alt = [torch.full((M, N), float("nan"), dtype=torch.bfloat16).share_memory_() for _ in range(world)]
+    mp.start_processes(_fused_worker, args=(world, _free_port(), M, N, K, ys, alt), nprocs=world,
                        start_method="spawn", join=True)
     from fack_b200 import data
     from fack_b200.dist import shard_weight
@@ -167,6 +188,7 @@ def test_fused_mode_two_gloo_ranks():
                        for r in range(world)], dim=1)
     for r in range(world):
         assert torch.equal(ys[r].view(torch.int16), exact.view(torch.int16)), f"rank {r}'s Y"
+        assert torch.equal(alt[r].view(torch.int16), exact.view(torch.int16)), f"rank {r}'s second Y"
 
 
 def test_fused_mode_contract():

@@ -270,6 +270,45 @@ def test_prefill_sampled_rows(cuda_device):
     assert_close(y[rows.to(d)], ref, "prefill rows")
 
 
+def _device_fp32_reference(xq, xs, wq, ws, row0=0, rows=None):
+    """The oracle's formula (driver.py:18-20) evaluated on the GPU in true fp32
+    (TF32 off): dequantise both operands, one fp32 matmul, bf16."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        sl = slice(row0, None if rows is None else row0 + rows)
+        a = xq[sl].float() * xs[sl].repeat_interleave(128, dim=1)
+        b = wq.float() * ws.repeat_interleave(128, dim=0).repeat_interleave(128, dim=1)
+        return (a @ b.T).bfloat16()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("workload", ["prefill", "wide_constant", "wide_uniform", "plumbing", "decode"])
+def test_full_output_vs_device_fp32(cuda_device, workload):
+    """Every element of the full-size benchmark configs, through the reference's
+    call form (pre-packed weight, transposed x_scale, the library's plan),
+    against the fp32 dequantise-then-matmul on the device (the CPU oracle
+    anchors the sampled-row / sampled-block tests above)."""
+    d = cuda_device
+    wl = data.WORKLOADS[workload]
+    xq, xs, wq, ws = data.make_inputs(wl, seed=0, device=d)
+    cfg = fb.get_config(wl.M, wl.N, wl.K)
+    out = poisoned(wl.M, wl.N, d)
+    fb.gemm_a8w8_blockscale_bpreshuffle_asm(xq, fb.shuffle_weight(wq), out, data.to_aiter_xscale(xs), ws, None,
+                                            cfg["splitK"], cfg["kernelName"], True)
+    torch.cuda.synchronize()
+    step = 2048  # rows per reference chunk: bounds the fp32 operands to ~0.6 GB
+    for r0 in range(0, wl.M, step):
+        n = min(step, wl.M - r0)
+        ref = _device_fp32_reference(xq, xs, wq, ws, r0, n)
+        y = out[r0:r0 + n].float()
+        assert torch.isfinite(y).all(), f"{workload}: unwritten output rows {r0}..{r0 + n}"
+        err = (y - ref.float()).abs()
+        bad = err > ATOL + RTOL * ref.float().abs()
+        assert not bad.any(), f"{workload} rows {r0}..: {int(bad.sum())} elements off, max {float(err.max()):.4g}"
+
+
 def test_prepack_layout_formula(cuda_device):
     """Packed tile (nb,kb) byte (r,c) sits at ((nb*KB+kb)*128 + r)*128 + ((c//16) ^ (r%8))*16 + c%16."""
     N, K = 256, 384

@@ -1,4 +1,4 @@
-"""CPU: the ctypes stubs shown in INTEGRATION.md (what a maintainer would
+"""CPU: the ctypes stubs of the integration guide (what a maintainer would
 paste into the reference's client) match the library's real signatures."""
 import ctypes
 import re

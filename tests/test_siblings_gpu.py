@@ -186,6 +186,41 @@ def test_public_entries_one_asm_call(cuda_device, name):
     assert torch.equal(y.view(torch.int16), want.view(torch.int16))
 
 
+@pytest.mark.parametrize("public,asm,dtype", [("gemm_a8w8_ASM", "gemm_a8w8_asm", torch.int8),
+                                              ("gemm_a16w16", "gemm_a16w16_asm", torch.bfloat16)])
+def test_public_entry_makes_exactly_one_asm_call(cuda_device, monkeypatch, public, asm, dtype):
+    """The reference's dispatch check (dispatch_driver.py:43-99) patches the
+    asm-level operator in the module the public entry resolves it from and
+    requires exactly one call with the configured kernelName and splitK; here
+    that module is fack_b200.siblings."""
+    d = cuda_device
+    M, N, K = 48, 512, 1024
+    g = torch.Generator().manual_seed(3)
+    if dtype == torch.int8:
+        a = torch.randint(-8, 9, (M, K), generator=g, dtype=torch.int8).to(d)
+        b = torch.randint(-8, 9, (N, K), generator=g, dtype=torch.int8).to(d)
+    else:
+        a = (0.1 * torch.randn((M, K), generator=g)).to(torch.bfloat16).to(d)
+        b = (0.1 * torch.randn((N, K), generator=g)).to(torch.bfloat16).to(d)
+    b = fb.shuffle_weight(b)
+    real = getattr(siblings, asm)
+    seen = []
+
+    def spy(*args, **kw):
+        seen.append(kw)
+        return real(*args, **kw)
+    monkeypatch.setattr(siblings, asm, spy)
+    if dtype == torch.int8:
+        sa, sb = torch.ones((M, 1), device=d), torch.ones((N, 1), device=d)
+        y = getattr(fb, public)(a, b, sa, sb, bias=None, dtype=torch.bfloat16)
+    else:
+        y = getattr(fb, public)(a, b, bias=None, otype=torch.bfloat16)
+    cfg = siblings.get_config(siblings.KINDS[dtype], M, N, K)
+    assert len(seen) == 1, f"{public} made {len(seen)} calls of {asm}"
+    assert seen[0]["kernelName"] == cfg["kernelName"] and seen[0]["splitK"] == cfg["splitK"]
+    assert y.shape == (M, N) and torch.isfinite(y.float()).all()
+
+
 def test_public_config_and_contract_errors(cuda_device):
     cfg = siblings.get_config(siblings.KINDS[torch.int8], 256, 3072, 7168)
     assert cfg["kernelName"].startswith("fack_tn_sm100_i8_t") and cfg["splitK"] >= 1
