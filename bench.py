@@ -267,7 +267,7 @@ def roofline(k_bytes, k_flops, k_us, peaks, clk, region_ms):
     return roof
 
 
-def measure_unsharded(name, steps, dev, stream, world, peaks, clk):
+def measure_unsharded(name, steps, dev, stream, world, peaks, local):
     """Kernel time of an unsharded workload on this rank's GPU (replicas when
     world > 1): CUDA-graph replays of the reference's call form over rotating
     input sets, max over ranks.  The secondary record of the bench line."""
@@ -291,19 +291,23 @@ def measure_unsharded(name, steps, dev, stream, world, peaks, clk):
     with torch.cuda.stream(stream):
         run = capture(lambda: [call(sets[i % n_sets]) for i in range(chunk)], stream, graphs)
     reps = max(3, math.ceil(steps / chunk))
+    sampler = ClockSampler(local)
+    sampler.start()
     timed_graph_replay([(run, 2)], stream)
     barrier(world)
     ms = max_over_ranks(timed_graph_replay([(run, reps)], stream), world, dev)
+    sampler.stop()
     for g in graphs:
         g.reset()
     us = ms * 1e3 / (reps * chunk)
+    clk = sampler.summary()
     roof = roofline(set_bytes, data.flops(wl.M, wl.N, wl.K), us, peaks, clk, ms)
     del sets
     return {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "kernel": cfg["kernelName"],
             "us_per_call": round(us, 3), "tflops": round(data.flops(wl.M, wl.N, wl.K) / (us * 1e6), 2),
             "hbm_gbs": round(set_bytes / (us * 1e3), 1), "calls_timed": reps * chunk,
             "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB", "roofline": roof,
-            "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+            "clocks": clk, "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
 
 
 def run_ours(args):
@@ -443,7 +447,7 @@ def run_ours(args):
     if args.workload != "decode" and not args.no_decode:
         del sets
         torch.cuda.empty_cache()
-        decode = measure_unsharded("decode", 2000, dev, stream, world, peaks, clk)
+        decode = measure_unsharded("decode", 2000, dev, stream, world, peaks, local)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -645,7 +649,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="prefill")

@@ -60,13 +60,14 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
 
 GEMM_LAUNCH_REGS = 168  # the FP8 kernel's setmaxnreg split is sized for this count
-GEMM_SPLIT_VARIANTS = 6  # gemm_bs_kernel<64|128|256, single CTA|pair>
+GEMM_SPLIT_VARIANTS = 9  # gemm_bs_kernel<64|128|256, single CTA|pair> + gemm_bs_persistent_kernel<64|128|256>
 
 
 def check_ptxas(log: str) -> None:
     """No kernel spills registers, and every variant of the register-split FP8
-    kernel (``gemm_bs_kernel``) uses exactly GEMM_LAUNCH_REGS registers, which
-    the host also checks before it launches one."""
+    kernels (``gemm_bs_kernel``, ``gemm_bs_persistent_kernel``) uses exactly
+    GEMM_LAUNCH_REGS registers, which the host also checks before it launches
+    one."""
     entry, found = None, 0
     for line in log.splitlines():
         m = re.search(r"Compiling entry function '(\S+)'", line)
@@ -79,12 +80,12 @@ def check_ptxas(log: str) -> None:
         if m and (int(m.group(1)) or int(m.group(2))):
             raise RuntimeError(f"{entry} spills registers: {line.strip()}")
         m = re.search(r"Used (\d+) registers", line)
-        if m and "gemm_bs_kernel" in entry:
+        if m and ("gemm_bs_kernel" in entry or "gemm_bs_persistent_kernel" in entry):
             found += 1
             if int(m.group(1)) != GEMM_LAUNCH_REGS:
                 raise RuntimeError(f"{entry} uses {m.group(1)} registers, expected {GEMM_LAUNCH_REGS}")
     if found != GEMM_SPLIT_VARIANTS:
-        raise RuntimeError(f"ptxas report lists {found} gemm_bs_kernel variants, expected {GEMM_SPLIT_VARIANTS}")
+        raise RuntimeError(f"ptxas report lists {found} register-split kernel variants, expected {GEMM_SPLIT_VARIANTS}")
 
 
 if __name__ == "__main__":

@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -739,6 +740,374 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   if (p.xchg) xchg_complete(p, status);
 }
 
+// ------------------------------------------------- persistent (multi-wave) --
+// Unsplit plans whose tiles outnumber the SMs (the prefill layer: 1792 tiles of
+// 128 x 256) run persistently: one CTA per SM walks its tiles (every
+// gridDim.x-th tile of the grouped launch order, so the tiles in flight at one
+// time still share operands in L2), and
+//  * the TMA producer and the MMA issuer run one continuous pipeline over all
+//    of the CTA's tiles and K blocks, so a tile's first loads and MMAs overlap
+//    the previous tile's last rescale and its epilogue;
+//  * the rescale warps hand each finished bf16 tile to a staging buffer of its
+//    own and go on with the next tile; two store warps (warps 2-3, idle in the
+//    one-tile kernel) copy it to Y -- and, for the fused all-gather, to every
+//    peer's Y over NVLink -- while the next tile computes;
+//  * barrier set-up, TMEM allocation and teardown happen once per SM, not
+//    once per tile.
+// The per-tile arithmetic (scales, paired FMA, bf16 rounding) is the one-tile
+// kernel's, so results are bitwise identical to it.
+constexpr int kPersistSmem = 232448 - 1024 - 256;   // dynamic budget minus alignment slack and misc
+
+template <int BN>
+struct PCfg {
+  static constexpr int kABytes = kTileM * kBlk;             // 16 KB token tile
+  static constexpr int kBBytes = BN * kBlk;                 // weight tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
+  static constexpr int kStgBytes = kTileM * kPitch16 * 2;   // one staged output tile
+  static constexpr int kRawBytes = 2 * kPrefetch * 256 * 4; // prefetched x_scale and w_scale slots
+  static constexpr int kFit = (kPersistSmem - kStgBytes - kRawBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kTmemBufs = (512 / BN) > 4 ? 4 : (512 / BN);
+  static constexpr int kTmemCols = kTmemBufs * BN;
+  static constexpr int kCpw = BN / 2;                       // columns per rescale warp
+  static constexpr bool kPairedFma = BN != 128;             // as in Cfg: the 128 tile keeps scalar FMAs
+  // columns per double-buffered TMEM load: 16 for the 256 tile, whose 128
+  // accumulator columns per thread leave no room for two 32-column buffers
+  // next to the tile loop's own state
+  static constexpr int kLdCols = BN == 256 ? 16 : 32;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kStages * kABytes;
+  static constexpr int kOffStg = kOffB + kStages * kBBytes;
+  static constexpr int kOffRaw = kOffStg + kStgBytes;
+  static constexpr int kOffRawW = kOffRaw + kPrefetch * 256 * 4;
+  static constexpr int kOffBar = kOffRawW + kPrefetch * 256 * 4;
+  static constexpr int kNumBars = 2 * kStages + 2 * kTmemBufs + 3;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+  static_assert(kStages >= 3, "persistent pipeline needs three stages");
+  static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+constexpr int kStoreWarp0 = 2;   // warps 2-3: store warps of the persistent kernel
+constexpr int kStoreThreads = 64;
+
+// i-th tile of this CTA in the grouped launch order (bands of kGroupM token
+// tiles, weight tiles outer within a band), as the one-tile kernel's remap.
+__device__ __forceinline__ void persistent_tile(int i, int n_tiles, int m_tiles, int& mt, int& nt) {
+  const int lin = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+  const int per_group = kGroupM * n_tiles;
+  const int g = lin / per_group;
+  const int first = g * kGroupM;
+  const int gm = min(kGroupM, m_tiles - first);
+  const int r = lin - g * per_group;
+  nt = r / gm;
+  mt = first + r % gm;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                          const __grid_constant__ Params p) {
+  using C = PCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int n_tiles = p.N / BN;
+  const int m_tiles = (p.M + kTileM - 1) / kTileM;
+  const int total = n_tiles * m_tiles;
+  const int my_tiles = total > static_cast<int>(blockIdx.x)
+                           ? (total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                           : 0;
+  const int KB = p.KB;
+
+  const uint32_t bar0 = base + C::kOffBar;
+  auto bar_full = [&](int i) { return bar0 + 8u * i; };
+  auto bar_empty = [&](int i) { return bar0 + 8u * (C::kStages + i); };
+  auto bar_tfull = [&](int i) { return bar0 + 8u * (2 * C::kStages + i); };
+  auto bar_tempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + C::kTmemBufs + i); };
+  const uint32_t bar_sfull = bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs);
+  const uint32_t bar_sempty = bar_sfull + 8u;
+  const uint32_t bar_drain = bar_sfull + 16u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(bar_full(i), 1);
+      mbar_init(bar_empty(i), 1);
+    }
+    for (int i = 0; i < C::kTmemBufs; ++i) {
+      mbar_init(bar_tfull(i), 1);
+      mbar_init(bar_tempty(i), 8);          // every rescale warp releases every buffer
+    }
+    mbar_init(bar_sfull, 8);                // the rescale warps have staged a tile
+    mbar_init(bar_sempty, 2);               // the store warps have drained it
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dependency_wait();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint64_t tmo = p.timeout_ns;
+  unsigned int* status = &g_status;
+  int produced = 0;
+
+  if (warp < kEpiWarp0) {
+    regs_dec<kCtrlRegs>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer --
+      if (lane == 0) {
+        const uint64_t pol_w = policy_evict_first();
+        const uint64_t pol_x = policy_evict_last();
+        int g = 0;
+        bool go = true;
+        for (int i = 0; i < my_tiles && go; ++i) {
+          int mt, nt;
+          persistent_tile(i, n_tiles, m_tiles, mt, nt);
+          const int m0 = mt * kTileM, n0 = nt * BN;
+          for (int kb = 0; kb < KB; ++kb, ++g) {
+            const int st = g % C::kStages;
+            const uint32_t ph = (g / C::kStages) & 1;
+            if (!wait_bounded(bar_empty(st), ph ^ 1u, abort_flag, status, kStProducer, tmo)) {
+              go = false;
+              break;
+            }
+            const uint32_t sa = base + C::kOffA + st * C::kABytes;
+            const uint32_t sb = base + C::kOffB + st * C::kBBytes;
+            mbar_arrive_expect_tx(bar_full(st), C::kStageBytes);
+            tma_load_2d(sa, &tmap_x, bar_full(st), kb * kBlk, m0, pol_x);
+            load_w_tile<BN>(sb, &tmap_w, bar_full(st), p, n0, kb, pol_w);
+            produced = g + 1;
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------------------------------------------------- MMA issuer --
+      if (lane == 0) {
+        constexpr uint32_t idesc = idesc_e4m3_f32(kTileM, BN);
+        const int n = my_tiles * KB;
+        for (int g = 0; g < n; ++g) {
+          const int st = g % C::kStages;
+          const uint32_t ph = (g / C::kStages) & 1;
+          const int buf = g % C::kTmemBufs;
+          const uint32_t bph = (g / C::kTmemBufs) & 1;
+          if (!wait_bounded(bar_tempty(buf), bph ^ 1u, abort_flag, status, kStMma, tmo)) break;
+          if (!wait_bounded(bar_full(st), ph, abort_flag, status, kStMma, tmo)) break;
+          tc_fence_after();
+          const uint32_t d = tmem_base + buf * BN;
+          const uint64_t da = sw128_kmajor_desc(base + C::kOffA + st * C::kABytes);
+          const uint64_t db = sw128_kmajor_desc(base + C::kOffB + st * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBlk / 32; ++k) umma_f8(d, da + 2 * k, db + 2 * k, idesc, k > 0 ? 1u : 0u);
+          umma_commit(bar_empty(st));
+          umma_commit(bar_tfull(buf));
+        }
+      }
+    } else {
+      // ---------------------------------------------------------- store warps --
+      const int t = threadIdx.x - kStoreWarp0 * 32;   // 0..63
+      constexpr int kRowChunks = BN / 8;               // 16-byte chunks per staged row
+      const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffStg);
+      for (int i = 0; i < my_tiles; ++i) {
+        const bool got = wait_bounded(bar_sfull, i & 1, abort_flag, status, kStEpilogue, tmo);
+        if (!__all_sync(0xffffffffu, got)) break;
+        int mt, nt;
+        persistent_tile(i, n_tiles, m_tiles, mt, nt);
+        const int m0 = mt * kTileM, n0 = nt * BN;
+        const int rows = min(kTileM, p.M - m0);
+        for (int c = t; c < rows * kRowChunks; c += kStoreThreads) {
+          const int r = c / kRowChunks, cc = c % kRowChunks;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
+          store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_sempty);
+      }
+      if (p.n_peer) __threadfence_system();
+    }
+  } else {
+    // -------------------------------------------------- rescale / epilogue --
+    regs_inc<kEpiRegs>();
+    const int q = warp & 3;
+    const int h = (warp - kEpiWarp0) >> 2;
+    const int col0 = h * C::kCpw;
+    const int tok = q * 32 + lane;
+    constexpr int kAccN = C::kPairedFma ? C::kCpw / 2 : C::kCpw;
+    using AccT = typename std::conditional<C::kPairedFma, uint64_t, float>::type;
+    AccT acc[kAccN];
+    auto acc_pair = [&](int j) -> float2 {
+      if constexpr (C::kPairedFma)
+        return unpack_f32x2(acc[j >> 1]);
+      else
+        return make_float2(acc[j], acc[j + 1]);
+    };
+    const int et = (warp - kEpiWarp0) * 32 + lane;
+    const uint32_t raw_x = base + C::kOffRaw + et * 4;
+    const uint32_t raw_w = base + C::kOffRawW + et * 4;
+    const float* raw_xp = reinterpret_cast<const float*>(smem + C::kOffRaw) + et;
+    const float* raw_wp = reinterpret_cast<const float*>(smem + C::kOffRawW) + et;
+    // Scale prefetch: a cursor (tile pi of this CTA, K block pkb) that runs
+    // kPrefetch K blocks ahead of the rescale; the tile's scale rows are
+    // looked up once per tile, and the flattened K block index pj picks the slot.
+    int pi = 0, pkb = 0, pj = 0;
+    bool phas = false;
+    const float* pxs = p.x_scale;
+    const float* pws = p.w_scale;
+    auto prefetch_tile = [&]() {
+      if (pi < my_tiles) {
+        int mt, nt;
+        persistent_tile(pi, n_tiles, m_tiles, mt, nt);
+        const int m = mt * kTileM + tok;
+        phas = m < p.M;
+        pxs = p.x_scale + static_cast<int64_t>(phas ? m : 0) * p.xs_sm;  // row 0 exists
+        pws = p.w_scale + static_cast<int64_t>((nt * BN + col0) >> 7) * KB;
+      }
+    };
+    auto prefetch = [&]() {
+      if (pi < my_tiles) {
+        const int off = (pj % kPrefetch) * 256 * 4;
+        cp_async4(raw_x + off, pxs + static_cast<int64_t>(pkb) * p.xs_sk, phas ? 4u : 0u);
+        cp_async4(raw_w + off, pws + pkb, 4u);
+        if (++pkb == KB) {
+          pkb = 0;
+          ++pi;
+          prefetch_tile();
+        }
+      }
+      ++pj;
+      cp_async_commit();  // one group per K block, empty past the end
+    };
+    prefetch_tile();
+#pragma unroll
+    for (int d = 0; d < kPrefetch; ++d) prefetch();
+    int g = 0;
+    bool done = true;
+    for (int i = 0; i < my_tiles && done; ++i) {
+#pragma unroll
+      for (int j = 0; j < kAccN; ++j) acc[j] = AccT(0);
+      for (int kb = 0; kb < KB; ++kb, ++g) {
+        const int buf = g % C::kTmemBufs;
+        const uint32_t bph = (g / C::kTmemBufs) & 1;
+        cp_async_wait<kPrefetch - 1>();
+        const float sc = raw_xp[(g % kPrefetch) * 256] * raw_wp[(g % kPrefetch) * 256];
+        const uint64_t sc2 = C::kPairedFma ? pack_f32x2(sc, sc) : 0ull;
+        prefetch();
+        const bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
+        if (!__all_sync(0xffffffffu, got)) {
+          done = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN + col0;
+        constexpr int kLd = C::kLdCols;
+        constexpr int kChunks = C::kCpw / kLd;
+        auto fold = [&](int c, const uint32_t(&v)[kLd]) {
+#pragma unroll
+          for (int t = 0; t < kLd; t += 2) {
+            if constexpr (C::kPairedFma) {
+              fma2_acc(acc[(c * kLd + t) >> 1], v[t], v[t + 1], sc2);
+            } else {
+              acc[c * kLd + t] = fmaf(__uint_as_float(v[t]), sc, acc[c * kLd + t]);
+              acc[c * kLd + t + 1] = fmaf(__uint_as_float(v[t + 1]), sc, acc[c * kLd + t + 1]);
+            }
+          }
+        };
+        auto ld_issue = [&](uint32_t addr, uint32_t(&v)[kLd]) {
+          if constexpr (kLd == 32) tmem_ld32_nowait(addr, v); else tmem_ld16_nowait(addr, v);
+        };
+        auto ld_wait = [&](uint32_t(&v)[kLd]) {
+          if constexpr (kLd == 32) tmem_wait32(v); else tmem_wait16(v);
+        };
+        uint32_t va[kLd], vb[kLd];
+        ld_issue(taddr, va);
+        ld_wait(va);
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          if ((c & 1) == 0) {
+            if (c + 1 < kChunks) ld_issue(taddr + (c + 1) * kLd, vb);
+            fold(c, va);
+            if (c + 1 < kChunks) ld_wait(vb);
+          } else {
+            if (c + 1 < kChunks) ld_issue(taddr + (c + 1) * kLd, va);
+            fold(c, vb);
+            if (c + 1 < kChunks) ld_wait(va);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty(buf));
+      }
+      if (!done) break;
+      // hand the tile to the store warps once they have drained the previous one
+      const bool free_stg = wait_bounded(bar_sempty, (i & 1) ^ 1, abort_flag, status, kStEpilogue, tmo);
+      if (!__all_sync(0xffffffffu, free_stg)) {
+        done = false;
+        break;
+      }
+      __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg) + tok * C::kPitch16 + col0;
+#pragma unroll
+      for (int j = 0; j < C::kCpw; j += 8) {
+        uint4 v;
+        const float2 f0 = acc_pair(j), f1 = acc_pair(j + 2);
+        const float2 f2 = acc_pair(j + 4), f3 = acc_pair(j + 6);
+        __nv_bfloat162 b0 = __floats2bfloat162_rn(f0.x, f0.y);
+        __nv_bfloat162 b1 = __floats2bfloat162_rn(f1.x, f1.y);
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(f2.x, f2.y);
+        __nv_bfloat162 b3 = __floats2bfloat162_rn(f3.x, f3.y);
+        v.x = *reinterpret_cast<uint32_t*>(&b0);
+        v.y = *reinterpret_cast<uint32_t*>(&b1);
+        v.z = *reinterpret_cast<uint32_t*>(&b2);
+        v.w = *reinterpret_cast<uint32_t*>(&b3);
+        *reinterpret_cast<uint4*>(row + j) = v;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfull);
+    }
+    cp_async_wait<0>();  // no copy may land after the CTA exits
+  }
+
+  // ------------------------------------------------------------ teardown --
+  grid_launch_dependents();
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();  // every role has left its loop; the store warps have drained every staged tile
+  tc_fence_after();
+  if (warp == 0) {
+    if (*abort_flag && lane == 0) {
+      const int first = produced > C::kStages ? produced - C::kStages : 0;
+      volatile int no_abort = 0;
+      for (int i = first; i < produced; ++i)
+        wait_bounded(bar_full(i % C::kStages), (i / C::kStages) & 1, &no_abort, status, kStDrain, tmo);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      umma_commit(bar_drain);
+      volatile int no_abort = 0;
+      wait_bounded(bar_drain, 0, &no_abort, status, kStDrain, tmo);
+    }
+    __syncwarp();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if (p.xchg) xchg_complete(p, status);
+}
+
 // ------------------------------------------------------ small-M (swapped) --
 // For M <= 64 tokens the operands swap sides: a CTA owns 128 weight rows
 // (the UMMA M side, TMEM lanes) x MT tokens (the N side, MT = 16/32/64 TMEM
@@ -1046,11 +1415,25 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 constexpr int kMaxDevices = 64;
 
-constexpr int kVariants = 9;  // weight tiles 64, 128, 256 x (single CTA, CTA pair) + swapped 16/32/64-token tiles
+// weight tiles 64, 128, 256 x (single CTA, CTA pair) + swapped 16/32/64-token
+// tiles + the persistent single-CTA kernel for weight tiles 64, 128, 256
+constexpr int kVariants = 12;
 
 static int variant(int tm, int bn) {
   if (tm < kTileM) return 6 + (tm == 16 ? 0 : tm == 32 ? 1 : 2);
   return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0);
+}
+static int persistent_variant(int bn) { return 9 + (bn == 64 ? 0 : bn == 128 ? 1 : 2); }
+
+// Unsplit 128-token plans with more tiles than SMs run on the persistent
+// kernel; FACK_PERSISTENT=0 in the environment keeps them on the one-tile
+// kernel (the two give bitwise identical results).
+static bool persistent_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FACK_PERSISTENT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 struct DeviceInfo {
@@ -1127,18 +1510,26 @@ static KernelEntry swap_entry() {
           false};
 }
 
-static const KernelEntry& kernel_for(int tm, int bn) {
-  static const KernelEntry table[kVariants] = {entry<64, false>(), entry<128, false>(), entry<256, false>(),
-                                               entry<64, true>(),  entry<128, true>(),  entry<256, true>(),
-                                               swap_entry<16>(),   swap_entry<32>(),    swap_entry<64>()};
-  return table[variant(tm, bn)];
+template <int BN>
+static KernelEntry persistent_entry() {
+  return {reinterpret_cast<const void*>(gemm_bs_persistent_kernel<BN>), PCfg<BN>::kSmemBytes, kThreads, true};
 }
 
-static int ensure_configured(DeviceInfo* d, int tm, int bn) {
-  const int v = variant(tm, bn);
+static const KernelEntry& kernel_by_variant(int v) {
+  static const KernelEntry table[kVariants] = {
+      entry<64, false>(),       entry<128, false>(),       entry<256, false>(),
+      entry<64, true>(),        entry<128, true>(),        entry<256, true>(),
+      swap_entry<16>(),         swap_entry<32>(),          swap_entry<64>(),
+      persistent_entry<64>(),   persistent_entry<128>(),   persistent_entry<256>()};
+  return table[v];
+}
+
+static const KernelEntry& kernel_for(int tm, int bn) { return kernel_by_variant(variant(tm, bn)); }
+
+static int ensure_variant(DeviceInfo* d, int v) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!(d->configured & (1u << v))) {
-    const KernelEntry& k = kernel_for(tm, bn);
+    const KernelEntry& k = kernel_by_variant(v);
     // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
     // launch; with any other count setmaxnreg.inc could wait forever, so the
     // kernel is refused instead of launched.
@@ -1154,6 +1545,8 @@ static int ensure_configured(DeviceInfo* d, int tm, int bn) {
   }
   return FACK_OK;
 }
+
+static int ensure_configured(DeviceInfo* d, int tm, int bn) { return ensure_variant(d, variant(tm, bn)); }
 
 // How many clusters of the (tm, bn) variant with `split` K slices the device
 // holds at once.  A cluster is (tm/128, 1, split) CTAs and must fit inside
@@ -1363,12 +1756,21 @@ static int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t
 
 static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CUtensorMap& tx, const Params& p,
                   int M, cudaStream_t stream) {
-  const int st = ensure_configured(d, tm, bn);
-  if (st != FACK_OK) return st;
-  const KernelEntry& k = kernel_for(tm, bn);
   int gx, gy, gz;
   plan_grid(M, p.N, tm, bn, p.split, &gx, &gy, &gz);
   if (gy > 65535 || gz > 65535) return fail(FACK_ERR_BAD_SHAPE, "problem too large for one launch (grid y > 65535)");
+  // more unsplit single-CTA tiles than SMs: one persistent CTA per SM
+  const bool persistent = tm == kTileM && p.split == 1 && persistent_enabled() &&
+                          static_cast<int64_t>(gx) * gy > d->sms;
+  const int v = persistent ? persistent_variant(bn) : variant(tm, bn);
+  const int st = ensure_variant(d, v);
+  if (st != FACK_OK) return st;
+  const KernelEntry& k = kernel_by_variant(v);
+  if (persistent) {
+    gx = d->sms;
+    gy = 1;
+    gz = 1;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gx, gy, gz);
   cfg.blockDim = dim3(k.threads, 1, 1);

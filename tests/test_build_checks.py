@@ -13,7 +13,8 @@ def entry(name, regs, spill_st=0, spill_ld=0):
             f"ptxas info    : Used {regs} registers, used 1 barriers, 900 bytes cmem[0]\n")
 
 
-SPLIT = [f"_ZN4fack14gemm_bs_kernelILi{bn}ELb{p}EEEv14CUtensorMap_st" for bn in (64, 128, 256) for p in (0, 1)]
+SPLIT = ([f"_ZN4fack14gemm_bs_kernelILi{bn}ELb{p}EEEv14CUtensorMap_st" for bn in (64, 128, 256) for p in (0, 1)] +
+         [f"_ZN4fack25gemm_bs_persistent_kernelILi{bn}EEEv14CUtensorMap_st" for bn in (64, 128, 256)])
 
 
 def clean():
@@ -38,6 +39,6 @@ def test_split_kernel_register_count_and_variant_count():
     bad = clean().replace(f"Used {build.GEMM_LAUNCH_REGS} registers", "Used 160 registers", 1)
     with pytest.raises(RuntimeError, match="expected 168"):
         build.check_ptxas(bad)
-    missing = "".join(entry(n, build.GEMM_LAUNCH_REGS) for n in SPLIT[:5])
-    with pytest.raises(RuntimeError, match="5 gemm_bs_kernel variants"):
+    missing = "".join(entry(n, build.GEMM_LAUNCH_REGS) for n in SPLIT[:-1])
+    with pytest.raises(RuntimeError, match=f"{len(SPLIT) - 1} register-split kernel variants"):
         build.check_ptxas(missing)

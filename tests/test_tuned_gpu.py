@@ -64,9 +64,9 @@ def shipped_rows():
 @pytest.mark.parametrize("row", shipped_rows(), ids=lambda r: f"{r['M']}x{r['N']}x{r['K']}")
 def test_shipped_rows_select_their_plan_and_match_oracle(cuda_device, row):
     """Every shipped row: the public entry takes the row's plan at the row's
-    shape; its whole output agrees with the fp32 dequantise-then-matmul on the
+    shape; its whole output agrees with the dequantise-then-matmul on the
     device and up to 24 evenly spaced rows with the CPU oracle."""
-    from test_gemm_gpu import _device_fp32_reference
+    from test_gemm_gpu import _device_reference
     M, N, K = int(row["M"]), int(row["N"]), int(row["K"])
     cu = torch.cuda.get_device_properties(0).multi_processor_count
     if int(row["cu_num"]) != cu:
@@ -76,7 +76,7 @@ def test_shipped_rows_select_their_plan_and_match_oracle(cuda_device, row):
     xq, xs = data.make_activations(M, K, "normal", 40 + M, device=d)
     wq, ws = data.make_weights(N, K, "normal", 41 + M, device=d)
     y = fb.gemm_a8w8_blockscale_bpreshuffle(xq, fb.shuffle_weight(wq), data.to_aiter_xscale(xs), ws)
-    assert_close(y, _device_fp32_reference(xq, xs, wq, ws), row["kernelName"] + " (device fp32)")
+    assert_close(y, _device_reference(xq, xs, wq, ws), row["kernelName"] + " (device reference)")
     rows = torch.linspace(0, M - 1, min(M, 24)).long().unique()
     ref = orc.reference_gemm(xq[rows.to(d)].cpu(), wq.cpu(), xs[rows.to(d)].cpu(), ws.cpu())
     assert_close(y[rows.to(d)], ref, row["kernelName"] + " (oracle rows)")
