@@ -454,9 +454,11 @@ def run_ours(args):
         tfl, cores, sample = cpu_oracle_rate(wl, budget_s=args.cpu_budget)
         cpu = {"value": round(tfl, 4), "unit": "TFLOPS", "cores": cores, "kind": "port", "sample": sample}
 
-    # GEMM launches per step: one (its last CTA runs the fused exchange), plus
-    # the interleave of the NCCL-gather path (NCCL's own kernels not counted)
-    per_step_launches = 2 if sharded and args.gather == "nccl" else 1
+    # our launches per step: the GEMM (plus the fix-up of its tail split when
+    # the plan has one; the last of them runs the fused exchange), plus the
+    # interleave of the NCCL-gather path (NCCL's own kernels not counted)
+    tail_split = cfg["splitK"] == 1 and fb.tail_workspace_size(wl.M, n_local, wl.K, cfg["tile_m"], cfg["tile_n"], 1) > 0
+    per_step_launches = (2 if tail_split else 1) + (1 if sharded and args.gather == "nccl" else 0)
     extra = sharder.barriers if sharder is not None and args.gather == "fused" else 0
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
@@ -466,7 +468,8 @@ def run_ours(args):
         "data": "synthetic (seeded; benchmark-config construction, scale = amax/240)",
         "config": {"workload": f"{wl.name} M={wl.M} N={wl.N} K={wl.K}", "M": wl.M, "N": wl.N, "K": wl.K,
                    "x_dist": wl.x_dist, "w_dist": wl.w_dist, "tile_m": cfg["tile_m"], "split_k": cfg["splitK"],
-                   "kernel": cfg["kernelName"], "n_local": n_local, "weights": "prepacked (bpreshuffle=True)",
+                   "kernel": cfg["kernelName"], "n_local": n_local, "tail_split": tail_split,
+                   "weights": "prepacked (bpreshuffle=True)",
                    "l2": f"rotate {n_sets} input sets x {set_bytes / 1e6:.1f} MB = {n_sets * set_bytes / 1e6:.0f} MB"
                          f" (> 126 MB L2)",
                    "timing": f"{timing}, CUDA events on the launch stream, max over ranks",

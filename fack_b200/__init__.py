@@ -19,6 +19,7 @@ from .ops import (  # noqa: F401
     get_config,
     quantize_activations,
     shuffle_weight,
+    tail_workspace_size,
     workspace_size,
 )
 from .siblings import gemm_a8w8_ASM, gemm_a8w8_asm, gemm_a16w16, gemm_a16w16_asm, gemm_tn  # noqa: F401
@@ -39,5 +40,6 @@ __all__ = [
     "get_config",
     "quantize_activations",
     "shuffle_weight",
+    "tail_workspace_size",
     "workspace_size",
 ]

@@ -61,6 +61,7 @@ SIGNATURES = {
                                      ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "fack_gemm_bs_plan_estimate": (_c_int, [_c_int] * 6 + [ctypes.POINTER(ctypes.c_double)]),
     "fack_gemm_bs_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_sz)]),
+    "fack_gemm_bs_tail_workspace_size": (_c_int, [_c_int] * 6 + [ctypes.POINTER(_c_sz)]),
     "fack_gemm_bs_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int),
                                    ctypes.POINTER(_c_int), ctypes.POINTER(_c_int), ctypes.POINTER(_c_sz)]),
     "fack_gemm_bs_ex": (_c_int, [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64,

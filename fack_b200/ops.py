@@ -35,10 +35,13 @@ Two layers:
 
 Every entry validates on the host and raises ``ValueError`` for a contract
 violation before launching, like the reference driver
-(client/aiter/hsa/gfx942/driver.py:11-12).  Calls allocate nothing: split-K
-slices are combined through the thread-block cluster's distributed shared
-memory (``reduce="global"`` instead uses a workspace cached per (device,
-stream), grown only outside CUDA-graph capture), so every call is
+(client/aiter/hsa/gfx942/driver.py:11-12).  Split-K slices are combined
+through the thread-block cluster's distributed shared memory
+(``reduce="global"`` instead uses a workspace cached per (device, stream)).
+A single-slice plan with more tiles than SMs runs persistently and takes the
+same cached workspace for its tail split (``tail=True``, the default).  A
+workspace grows only outside CUDA-graph capture -- during capture a call that
+would need a larger one runs its plan unsplit instead -- so every call is
 capturable.
 """
 from __future__ import annotations
@@ -142,6 +145,36 @@ def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
     return ws
 
 
+_tail_sizes: dict = {}
+
+
+def tail_workspace_size(M: int, N: int, K: int, tile_m: int = 0, tile_n: int = 0, split_k: int = 0) -> int:
+    """Bytes of the optional workspace that lets a single-slice plan spread its
+    last partial round of tiles over all SMs (fack_gemm_bs_tail_workspace_size);
+    0 when the plan has no such tail.  Cached per device and shape."""
+    key = (torch.cuda.current_device(), M, N, K, tile_m, tile_n, split_k)
+    nb = _tail_sizes.get(key)
+    if nb is None:
+        lib = _lib.load()
+        b = ctypes.c_size_t()
+        _lib.check(lib.fack_gemm_bs_tail_workspace_size(int(M), int(N), int(K), int(tile_m), int(tile_n),
+                                                        int(split_k), ctypes.byref(b)),
+                   "fack_gemm_bs_tail_workspace_size")
+        nb = _tail_sizes[key] = b.value
+    return nb
+
+
+def _tail_workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
+    """The cached workspace for a tail split, or None (the launch then runs
+    unsplit) when it would have to grow during CUDA-graph capture."""
+    if nbytes == 0:
+        return None
+    ws = _workspaces.get((device.index, _stream_handle(device)))
+    if torch.cuda.is_current_stream_capturing() and (ws is None or ws.numel() < nbytes):
+        return None
+    return _workspace(device, nbytes)
+
+
 def _check_common(xq, wq, w_scale, out, M, N, K):
     for name, t in (("XQ", xq), ("WQ", wq), ("w_scale", w_scale), ("out", out)):
         if not isinstance(t, torch.Tensor) or not t.is_cuda:
@@ -164,10 +197,13 @@ def _check_common(xq, wq, w_scale, out, M, N, K):
 
 
 def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m=0, tile_n=0,
-            reduce="dsmem", peer_outs=(), xchg=None):
+            reduce="dsmem", peer_outs=(), xchg=None, tail=True):
     """reduce = "dsmem": split-K slices combine through the cluster's shared
     memory (no workspace, nothing allocated); "global": through a cached
-    workspace in global memory.  ``peer_outs``: device addresses (this
+    workspace in global memory.  ``tail``: a single-slice plan whose tiles
+    outnumber the SMs gets the cached workspace for its tail split
+    (:func:`tail_workspace_size`; grown outside CUDA-graph capture only,
+    else the launch runs unsplit).  ``peer_outs``: device addresses (this
     process's mappings of other GPUs' memory) of more copies of ``out``'s
     block, same row stride; every result is stored to each of them too.
     ``xchg`` (with ``peer_outs`` for every other rank, in rank order): the
@@ -180,7 +216,10 @@ def _launch(xq, wq, packed, x_scale, xs_sm, xs_sk, w_scale, out, split_k, tile_m
     lib = _lib.load()
     with torch.cuda.device(dev):
         tm, tn, sk, need = plan(M, N, K, tile_m, tile_n, split_k)
-        ws = _workspace(dev, need) if reduce == "global" else None
+        if sk > 1:
+            ws = _workspace(dev, need) if reduce == "global" else None
+        else:
+            ws = _tail_workspace(dev, tail_workspace_size(M, N, K, tm, tn, sk)) if tail else None
         args = (xq.data_ptr(), xq.stride(0), wq.data_ptr(), _lib.FACK_W_PACKED if packed else _lib.FACK_W_ROW_MAJOR,
                 x_scale.data_ptr(), int(xs_sm), int(xs_sk), w_scale.data_ptr(), out.data_ptr(), out.stride(0))
         tail = (M, N, K, tm, tn, sk, _ptr(ws), 0 if ws is None else ws.numel(), _stream_handle(dev))
@@ -217,7 +256,7 @@ def xchg_barrier(xchg, device) -> None:
 
 def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor,
                     out: Optional[torch.Tensor] = None, split_k: int = 0, tile_n: int = 0, tile_m: int = 0,
-                    reduce: str = "dsmem", peer_outs=(), xchg=None) -> torch.Tensor:
+                    reduce: str = "dsmem", peer_outs=(), xchg=None, tail: bool = True) -> torch.Tensor:
     """Y = blockscale(XQ, WQ) with x_scale read through its logical strides.
 
     ``wq`` may be a row-major ``[N, K]`` e4m3 tensor or the output of
@@ -228,6 +267,8 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
     ``xchg`` as well (one peer output per other rank, the exchange state of
     :class:`fack_b200.dist.ExchangeState`) the launch also waits, on the
     device, until every rank's block has landed (``fack_gemm_bs_allgather``).
+    ``tail=False`` keeps a persistent plan's last partial round of tiles
+    unsplit (no workspace).
     """
     if len(peer_outs) > 7:
         raise ValueError("at most 7 peer outputs")
@@ -248,7 +289,7 @@ def gemm_blockscale(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w
     if reduce not in ("dsmem", "global"):
         raise ValueError("reduce must be 'dsmem' or 'global'")
     return _launch(xq, wq, bool(getattr(wq, "is_shuffled", False)), x_scale, sm, sk, w_scale, out, split_k, tile_m,
-                   tile_n, reduce, tuple(peer_outs), xchg)
+                   tile_n, reduce, tuple(peer_outs), xchg, tail)
 
 
 def _aiter_xscale_strides(x_scale: torch.Tensor, M: int, KB: int):

@@ -317,13 +317,33 @@ int fack_gemm_bs(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                  void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Optional workspace of a single-slice plan (split_k resolves to 1, 128-token
+ * tiles) whose tiles outnumber the current device's SMs.  Such a plan runs on
+ * one persistent CTA per SM, and T tiles on G SMs leave a last round of
+ * T mod G tiles (1792 = 12 x 148 + 16 for the prefill layer) during which
+ * most SMs idle.  Given a workspace of at least *bytes (16-byte aligned) in
+ * fack_gemm_bs / fack_gemm_bs_ex, those last tiles are cut into 2..8 K slices
+ * spread over the idle SMs; each slice writes an fp32 partial there and a
+ * second, small launch in the same stream sums the slices in a fixed order
+ * (deterministic) and stores the bf16 tiles.  Without the workspace (NULL or
+ * smaller) the plan runs unsplit.  The two results differ only in the fp32
+ * summation order of those tiles.  *bytes = 0 when the plan has no such tail.
+ * Same tile / split requests as fack_gemm_bs_plan; queries the current device.
+ * No counterpart in the reference (its tile kernels are not persistent).
+ */
+int fack_gemm_bs_tail_workspace_size(int M, int N, int K, int tile_m_request, int tile_n_request,
+                                     int split_k_request, size_t* bytes);
+
+/*
  * fack_gemm_bs with an explicit plan (tile_m, tile_n, split_k; 0 = library
  * choice), the counterpart of aiter selecting one tile kernel by kernelName
  * (client/aiter/hsa/gfx942/driver.py:26-29 passes kernelName=symbol).
  * For split_k > 1 the K slices of a tile are combined either through the
  * caller's workspace (when `workspace` is not NULL; at least the plan's
  * workspace bytes) or, with workspace = NULL, through the distributed shared
- * memory of the tile's thread-block cluster (no global memory).
+ * memory of the tile's thread-block cluster (no global memory).  For a
+ * single-slice plan the workspace is optional and enables the tail split of
+ * fack_gemm_bs_tail_workspace_size when it is large enough.
  */
 int fack_gemm_bs_ex(const void* xq, int64_t ldx, const void* wq, int wq_packed,
                     const float* x_scale, int64_t xs_stride_m, int64_t xs_stride_kb,

@@ -19,7 +19,8 @@ def main(out_path):
     res = {}
     for name, (M, N, K, tn) in CASES.items():
         xq, xs, wq, ws = inputs(M, N, K, d)
-        res[name] = fb.gemm_blockscale(xq, fb.shuffle_weight(wq), xs, ws, tile_n=tn, tile_m=128, split_k=1).cpu()
+        res[name] = fb.gemm_blockscale(xq, fb.shuffle_weight(wq), xs, ws, tile_n=tn, tile_m=128, split_k=1,
+                                       tail=False).cpu()
     torch.save(res, out_path)
 
 

@@ -29,4 +29,8 @@ def test_sharded_gemm_gpus(world):
            str(ROOT / "tests" / "_dist_gpu_worker.py")]
     env = dict(os.environ)
     res = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, env=env)
+    log = os.environ.get("FACK_DIST_LOG")   # optional: keep the per-case records (plans, timings, errors)
+    if log:
+        with open(log, "a") as f:
+            f.writelines(ln[len("DIST_CASE "):] + "\n" for ln in res.stdout.splitlines() if ln.startswith("DIST_CASE "))
     assert res.returncode == 0 and "DIST_GPU_OK" in res.stdout, res.stdout[-4000:] + res.stderr[-3000:]

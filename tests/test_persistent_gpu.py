@@ -1,8 +1,11 @@
 """GPU: the persistent kernel (unsplit 128-token plans with more tiles than
 SMs: one CTA per SM walks its tiles while two store warps drain the previous
-tile) gives the same bits as the one-tile kernel, which a subprocess runs with
-FACK_PERSISTENT=0, and agrees with the oracle on sampled rows; every output
-element is written (NaN poison)."""
+tile).  Without a tail split it gives the same bits as the one-tile kernel,
+which a subprocess runs with FACK_PERSISTENT=0.  With the tail split (the last
+T mod G tiles cut into K slices, summed by a fix-up launch) every element
+agrees with the dequantise-then-matmul reference, the result is bitwise
+reproducible, and it differs from the unsplit result only inside the tail
+tiles.  Every output element is written (NaN poison)."""
 import os
 import subprocess
 import sys
@@ -12,9 +15,9 @@ import pytest
 import torch
 
 import fack_b200 as fb
+from _persistent_cases import CASES, grouped_tile, inputs
 from oracle.blockscale import reference_gemm
-from _persistent_cases import CASES, inputs
-from test_gemm_gpu import assert_close
+from test_gemm_gpu import _device_reference, assert_close
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
@@ -30,14 +33,20 @@ def one_tile_outputs(tmp_path_factory, cuda_device):
     return torch.load(path)
 
 
+def run(case, dev, tail):
+    M, N, K, tn = CASES[case]
+    xq, xs, wq, ws = inputs(M, N, K, dev)
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+    fb.gemm_blockscale(xq, fb.shuffle_weight(wq), xs, ws, out=out, tile_n=tn, tile_m=128, split_k=1, tail=tail)
+    torch.cuda.synchronize()
+    return out, (xq, xs, wq, ws)
+
+
 @pytest.mark.parametrize("name", list(CASES))
 def test_persistent_matches_one_tile_kernel(cuda_device, one_tile_outputs, name):
     M, N, K, tn = CASES[name]
     assert (M + 127) // 128 * (N // tn) > torch.cuda.get_device_properties(0).multi_processor_count
-    xq, xs, wq, ws = inputs(M, N, K, cuda_device)
-    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda_device)
-    fb.gemm_blockscale(xq, fb.shuffle_weight(wq), xs, ws, out=out, tile_n=tn, tile_m=128, split_k=1)
-    torch.cuda.synchronize()
+    out, (xq, xs, wq, ws) = run(name, cuda_device, tail=False)
     y = out.cpu()
     assert torch.isfinite(y.float()).all(), "unwritten output elements"
     ref = one_tile_outputs[name]
@@ -46,4 +55,32 @@ def test_persistent_matches_one_tile_kernel(cuda_device, one_tile_outputs, name)
     rows = torch.linspace(0, M - 1, 12).long()
     assert_close(y[rows], reference_gemm(xq[rows.to(cuda_device)].cpu(), wq.cpu(), xs[rows.to(cuda_device)].cpu(),
                                          ws.cpu()), name)
+    assert fb.device_status() == 0
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_tail_split(cuda_device, name):
+    M, N, K, tn = CASES[name]
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    m_tiles, n_tiles = (M + 127) // 128, N // tn
+    T = m_tiles * n_tiles
+    rem = T % sms
+    split = min(8, sms // rem if rem else 0, K // 128 // 2)
+    nb = fb.tail_workspace_size(M, N, K, 128, tn, 1)
+    assert nb == (rem * split * 128 * tn * 4 if split >= 2 else 0), (nb, rem, split)
+    y1, (xq, xs, wq, ws) = run(name, cuda_device, tail=True)
+    y2, _ = run(name, cuda_device, tail=True)
+    assert torch.isfinite(y1.float()).all(), "unwritten output elements"
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16)), "tail split not bitwise reproducible"
+    assert_close(y1, _device_reference(xq, xs, wq, ws), name + " tail split")
+    plain, _ = run(name, cuda_device, tail=False)
+    diff = (y1.view(torch.int16) != plain.view(torch.int16))
+    if nb == 0:
+        assert not diff.any()
+    else:
+        tail_mask = torch.zeros((M, N), dtype=torch.bool, device=cuda_device)
+        for lin in range(T - rem, T):
+            mt, nt = grouped_tile(lin, n_tiles, m_tiles)
+            tail_mask[mt * 128:(mt + 1) * 128, nt * tn:(nt + 1) * tn] = True
+        assert not (diff & ~tail_mask).any(), "a tile outside the tail changed with the tail split"
     assert fb.device_status() == 0
