@@ -768,8 +768,11 @@ struct PCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kPitch16 = BN + 8;                   // bf16 staging pitch (elements)
   static constexpr int kStgBytes = kTileM * kPitch16 * 2;   // one staged output tile
+  // two staging buffers where shared memory allows (weight tiles up to 128):
+  // the store warps then drain tile i while tile i + 1 is staged
+  static constexpr int kStgBufs = BN <= 128 ? 2 : 1;
   static constexpr int kRawBytes = 2 * kPrefetch * 256 * 4; // prefetched x_scale and w_scale slots
-  static constexpr int kFit = (kPersistSmem - kStgBytes - kRawBytes) / kStageBytes;
+  static constexpr int kFit = (kPersistSmem - kStgBufs * kStgBytes - kRawBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kTmemBufs = (512 / BN) > 4 ? 4 : (512 / BN);
   static constexpr int kTmemCols = kTmemBufs * BN;
@@ -782,10 +785,10 @@ struct PCfg {
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kStages * kABytes;
   static constexpr int kOffStg = kOffB + kStages * kBBytes;
-  static constexpr int kOffRaw = kOffStg + kStgBytes;
+  static constexpr int kOffRaw = kOffStg + kStgBufs * kStgBytes;
   static constexpr int kOffRawW = kOffRaw + kPrefetch * 256 * 4;
   static constexpr int kOffBar = kOffRawW + kPrefetch * 256 * 4;
-  static constexpr int kNumBars = 2 * kStages + 2 * kTmemBufs + 3;
+  static constexpr int kNumBars = 2 * kStages + 2 * kTmemBufs + 2 * kStgBufs + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
   static_assert(kStages >= 3, "persistent pipeline needs three stages");
@@ -864,9 +867,10 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
   auto bar_empty = [&](int i) { return bar0 + 8u * (C::kStages + i); };
   auto bar_tfull = [&](int i) { return bar0 + 8u * (2 * C::kStages + i); };
   auto bar_tempty = [&](int i) { return bar0 + 8u * (2 * C::kStages + C::kTmemBufs + i); };
-  const uint32_t bar_sfull = bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs);
-  const uint32_t bar_sempty = bar_sfull + 8u;
-  const uint32_t bar_drain = bar_sfull + 16u;
+  // staging buffer b: full (staged by the rescale warps), empty (drained)
+  auto bar_sfull = [&](int b) { return bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs + b); };
+  auto bar_sempty = [&](int b) { return bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs + C::kStgBufs + b); };
+  const uint32_t bar_drain = bar0 + 8u * (2 * C::kStages + 2 * C::kTmemBufs + 2 * C::kStgBufs);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
@@ -879,8 +883,10 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
       mbar_init(bar_tfull(i), 1);
       mbar_init(bar_tempty(i), 8);          // every rescale warp releases every buffer
     }
-    mbar_init(bar_sfull, 8);                // the rescale warps have staged a tile
-    mbar_init(bar_sempty, 2);               // the store warps have drained it
+    for (int b = 0; b < C::kStgBufs; ++b) {
+      mbar_init(bar_sfull(b), 8);           // the rescale warps have staged a tile
+      mbar_init(bar_sempty(b), 2);          // the store warps' copies have read it
+    }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -960,24 +966,43 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
       }
     } else {
       // ---------------------------------------------------------- store warps --
+      // Each staged row (BN bf16, contiguous in Y) goes to Y and to every peer's
+      // Y as one bulk copy by the TMA engine, so many rows per destination are
+      // in flight at once (16-byte stores from two warps kept too few in
+      // flight to feed NVLink at 8 GPUs).  The staging buffer is handed back
+      // once the copies have read it.
       const int t = threadIdx.x - kStoreWarp0 * 32;   // 0..63
-      constexpr int kRowChunks = BN / 8;               // 16-byte chunks per staged row
-      const __nv_bfloat16* stg = reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffStg);
+      constexpr uint32_t kRowBytes = BN * 2;
+      constexpr int B = C::kStgBufs;
       for (int i = 0; i < w.n_dp; ++i) {
-        const bool got = wait_bounded(bar_sfull, i & 1, abort_flag, status, kStEpilogue, tmo);
+        const bool got = wait_bounded(bar_sfull(i % B), (i / B) & 1, abort_flag, status, kStEpilogue, tmo);
         if (!__all_sync(0xffffffffu, got)) break;
         int mt, nt, kb0, kb1;
         w.item(p, i, mt, nt, kb0, kb1);
         const int m0 = mt * kTileM, n0 = nt * BN;
         const int rows = min(kTileM, p.M - m0);
-        for (int c = t; c < rows * kRowChunks; c += kStoreThreads) {
-          const int r = c / kRowChunks, cc = c % kRowChunks;
-          const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
-          store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
+        const uint32_t stg = base + C::kOffStg + (i % B) * C::kStgBytes;
+        for (int r = t; r < rows; r += kStoreThreads) {
+          const uint32_t src = stg + static_cast<uint32_t>(r * C::kPitch16 * 2);
+          const int64_t off = static_cast<int64_t>(m0 + r) * p.ldo + n0;
+          for (int d = 0; d < p.n_peer; ++d) bulk_store_s2g(p.peer_out[d] + off, src, kRowBytes);
+          bulk_store_s2g(p.out + off, src, kRowBytes);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_sempty);
+        bulk_commit();
+        if constexpr (B == 1) {
+          bulk_wait_read_all();  // the staging buffer may be overwritten
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_sempty(0));
+        } else if (i >= 1) {
+          // tile i's copies are queued; hand back the previous tile's buffer
+          // once its copies have read it
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_sempty((i - 1) % B));
+        }
       }
+      bulk_wait_all();            // every row has landed in Y and the peers' Y ...
+      fence_proxy_async_global();  // ... before this thread's later fences and stores
       if (p.n_peer) __threadfence_system();
     }
   } else {
@@ -1109,13 +1134,15 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
         }
         continue;
       }
-      // hand the tile to the store warps once they have drained the previous one
-      const bool free_stg = wait_bounded(bar_sempty, (i & 1) ^ 1, abort_flag, status, kStEpilogue, tmo);
+      // hand the tile to the store warps once they have drained this buffer
+      constexpr int B = C::kStgBufs;
+      const bool free_stg = wait_bounded(bar_sempty(i % B), ((i / B) & 1) ^ 1, abort_flag, status, kStEpilogue, tmo);
       if (!__all_sync(0xffffffffu, free_stg)) {
         done = false;
         break;
       }
-      __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg) + tok * C::kPitch16 + col0;
+      __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg + (i % B) * C::kStgBytes) +
+                           tok * C::kPitch16 + col0;
 #pragma unroll
       for (int j = 0; j < C::kCpw; j += 8) {
         uint4 v;
@@ -1131,8 +1158,9 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
         v.w = *reinterpret_cast<uint32_t*>(&b3);
         *reinterpret_cast<uint4*>(row + j) = v;
       }
+      fence_proxy_async_smem();  // the staged row is read by the TMA engine (bulk copies)
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_sfull);
+      if (lane == 0) mbar_arrive(bar_sfull(i % B));
     }
     cp_async_wait<0>();  // no copy may land after the CTA exits
   }
