@@ -133,3 +133,12 @@ def test_quantize_activations_refuses_before_launch():
         fb.quantize_activations(torch.zeros(4, 256))
     with pytest.raises(ValueError, match="2-D"):
         fb.quantize_activations(torch.zeros(256))
+
+
+def test_case_bench_cli_without_a_device():
+    """The ncu case driver parses its arguments and refuses to run without a GPU."""
+    import torch
+    from fack_b200 import case_bench
+    if torch.cuda.is_available():
+        return
+    assert case_bench.main(["256", "3072", "7168", "--plan", "128,256,5"]) == 2
