@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
 
 GEMM_LAUNCH_REGS = 168  # the FP8 kernel's setmaxnreg split is sized for this count
-GEMM_SPLIT_VARIANTS = 9  # gemm_bs_kernel<64|128|256, single CTA|pair> + gemm_bs_persistent_kernel<64|128|256>
+GEMM_SPLIT_VARIANTS = 10  # gemm_bs_kernel<64|128|256, single CTA|pair> + gemm_bs_persistent_kernel<64|128|224|256>
 
 
 def check_ptxas(log: str) -> None:

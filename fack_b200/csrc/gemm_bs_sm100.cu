@@ -296,13 +296,24 @@ __device__ __noinline__ void reduce_global(const float* part0, const float* stg,
 // TMA of one K block of a BN-row weight tile starting at weight row wr0:
 // packed layout (tile (nb, kb) is 128 rows x 128 B at row (nb*KB + kb)*128)
 // or row-major [N, K].
+// A 224-row tile (first row a multiple of 32, not of 128) is loaded from the
+// packed layout as seven 32-row boxes, each inside one packed 128-row tile
+// (the host encodes 32-row boxes for it).
 template <int WROWS>
 __device__ __forceinline__ void load_w_tile(uint32_t dst, const CUtensorMap* map, uint32_t bar, const Params& p,
                                             int wr0, int kb, uint64_t pol) {
   if (p.w_packed) {
+    if constexpr (WROWS == 224) {
 #pragma unroll
-    for (int t = 0; t < (WROWS + 127) / 128; ++t)
-      tma_load_2d(dst + t * 16384, map, bar, 0, (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol);
+      for (int j = 0; j < WROWS / 32; ++j) {
+        const int r = wr0 + 32 * j;
+        tma_load_2d(dst + j * 4096, map, bar, 0, ((r >> 7) * p.KB + kb) * kBlk + (r & 127), pol);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < (WROWS + 127) / 128; ++t)
+        tma_load_2d(dst + t * 16384, map, bar, 0, (((wr0 >> 7) + t) * p.KB + kb) * kBlk + (wr0 & 127), pol);
+    }
   } else {
     tma_load_2d(dst, map, bar, kb * kBlk, wr0, pol);
   }
@@ -771,23 +782,29 @@ struct PCfg {
   // two staging buffers where shared memory allows (weight tiles up to 128):
   // the store warps then drain tile i while tile i + 1 is staged
   static constexpr int kStgBufs = BN <= 128 ? 2 : 1;
-  static constexpr int kRawBytes = 2 * kPrefetch * 256 * 4; // prefetched x_scale and w_scale slots
+  // w_scale values per thread and K block: a 224-row tile's half (112 rows)
+  // may span two 128-row scale blocks
+  static constexpr int kWScales = BN == 224 ? 2 : 1;
+  static constexpr int kRawBytes = (1 + kWScales) * kPrefetch * 256 * 4; // prefetched x_scale and w_scale slots
   static constexpr int kFit = (kPersistSmem - kStgBufs * kStgBytes - kRawBytes) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kTmemBufs = (512 / BN) > 4 ? 4 : (512 / BN);
-  static constexpr int kTmemCols = kTmemBufs * BN;
+  // the allocation is a power of two: 2 x 224 columns take 512
+  static constexpr int kTmemCols = kTmemBufs * BN <= 256 ? 256 : 512;
   static constexpr int kCpw = BN / 2;                       // columns per rescale warp
   static constexpr bool kPairedFma = BN != 128;             // as in Cfg: the 128 tile keeps scalar FMAs
-  // columns per double-buffered TMEM load: 16 for the 256 tile, whose 128
-  // accumulator columns per thread leave no room for two 32-column buffers
-  // next to the tile loop's own state
-  static constexpr int kLdCols = BN == 256 ? 16 : 32;
+  // columns per double-buffered TMEM load: 16 for the 256 and 224 tiles,
+  // whose 128 / 112 accumulator columns per thread leave no room for two
+  // 32-column buffers next to the tile loop's own state
+  static constexpr int kLdCols = BN >= 224 ? 16 : 32;
+
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kStages * kABytes;
   static constexpr int kOffStg = kOffB + kStages * kBBytes;
   static constexpr int kOffRaw = kOffStg + kStgBufs * kStgBytes;
   static constexpr int kOffRawW = kOffRaw + kPrefetch * 256 * 4;
-  static constexpr int kOffBar = kOffRawW + kPrefetch * 256 * 4;
+  static constexpr int kOffRawW2 = kOffRawW + kPrefetch * 256 * 4;   // second w_scale (224 tile only)
+  static constexpr int kOffBar = kOffRawW + kWScales * kPrefetch * 256 * 4;
   static constexpr int kNumBars = 2 * kStages + 2 * kTmemBufs + 2 * kStgBufs + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
@@ -1024,16 +1041,20 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
     const int et = (warp - kEpiWarp0) * 32 + lane;
     const uint32_t raw_x = base + C::kOffRaw + et * 4;
     const uint32_t raw_w = base + C::kOffRawW + et * 4;
+    const uint32_t raw_w2 = base + C::kOffRawW2 + et * 4;
     const float* raw_xp = reinterpret_cast<const float*>(smem + C::kOffRaw) + et;
     const float* raw_wp = reinterpret_cast<const float*>(smem + C::kOffRawW) + et;
+    const float* raw_w2p = reinterpret_cast<const float*>(smem + C::kOffRawW2) + et;
     // Scale prefetch: a cursor (item pi of this CTA, K block pkb of its range
     // [pkb0, pkb1)) that runs kPrefetch K blocks ahead of the rescale; an
     // item's scale rows are looked up once, and the flattened K block index
-    // pj picks the slot.
+    // pj picks the slot.  pws2: the scale block of this thread's last column
+    // (the 224 tile's halves can span two blocks).
     int pi = 0, pkb = 0, pkb1 = 0, pj = 0;
     bool phas = false;
     const float* pxs = p.x_scale;
     const float* pws = p.w_scale;
+    const float* pws2 = p.w_scale;
     auto prefetch_item = [&]() {
       if (pi < w.my_items) {
         int mt, nt, kb0, kb1;
@@ -1042,6 +1063,7 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
         phas = m < p.M;
         pxs = p.x_scale + static_cast<int64_t>(phas ? m : 0) * p.xs_sm;  // row 0 exists
         pws = p.w_scale + static_cast<int64_t>((nt * BN + col0) >> 7) * w.KB;
+        pws2 = p.w_scale + static_cast<int64_t>((nt * BN + col0 + C::kCpw - 1) >> 7) * w.KB;
         pkb = kb0;
         pkb1 = kb1;
       }
@@ -1051,6 +1073,7 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
         const int off = (pj % kPrefetch) * 256 * 4;
         cp_async4(raw_x + off, pxs + static_cast<int64_t>(pkb) * p.xs_sk, phas ? 4u : 0u);
         cp_async4(raw_w + off, pws + pkb, 4u);
+        if constexpr (C::kWScales == 2) cp_async4(raw_w2 + off, pws2 + pkb, 4u);
         if (++pkb == pkb1) {
           ++pi;
           prefetch_item();
@@ -1067,14 +1090,21 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
     for (int i = 0; i < w.my_items && done; ++i) {
       int mt, nt, kb0, kb1;
       w.item(p, i, mt, nt, kb0, kb1);
+      // columns of this thread's half before the next 128-row scale block
+      // (only the 224 tile's halves cross one: chunks from there on take the
+      // second scale)
+      const int cross = C::kWScales == 2 ? 128 - ((nt * BN + col0) & 127) : C::kCpw;
 #pragma unroll
       for (int j = 0; j < kAccN; ++j) acc[j] = AccT(0);
       for (int kb = kb0; kb < kb1; ++kb, ++g) {
         const int buf = g % C::kTmemBufs;
         const uint32_t bph = (g / C::kTmemBufs) & 1;
         cp_async_wait<kPrefetch - 1>();
-        const float sc = raw_xp[(g % kPrefetch) * 256] * raw_wp[(g % kPrefetch) * 256];
+        const float xsc = raw_xp[(g % kPrefetch) * 256];
+        const float sc = xsc * raw_wp[(g % kPrefetch) * 256];
+        const float sc_hi = C::kWScales == 2 ? xsc * raw_w2p[(g % kPrefetch) * 256] : sc;
         const uint64_t sc2 = C::kPairedFma ? pack_f32x2(sc, sc) : 0ull;
+        const uint64_t sc2_hi = C::kPairedFma ? pack_f32x2(sc_hi, sc_hi) : 0ull;
         prefetch();
         const bool got = wait_bounded(bar_tfull(buf), bph, abort_flag, status, kStEpilogue, tmo);
         if (!__all_sync(0xffffffffu, got)) {
@@ -1086,10 +1116,11 @@ gemm_bs_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __gr
         constexpr int kLd = C::kLdCols;
         constexpr int kChunks = C::kCpw / kLd;
         auto fold = [&](int c, const uint32_t(&v)[kLd]) {
+          const bool hi = c * kLd >= cross;
 #pragma unroll
           for (int t = 0; t < kLd; t += 2) {
             if constexpr (C::kPairedFma) {
-              fma2_acc(acc[(c * kLd + t) >> 1], v[t], v[t + 1], sc2);
+              fma2_acc(acc[(c * kLd + t) >> 1], v[t], v[t + 1], hi ? sc2_hi : sc2);
             } else {
               acc[c * kLd + t] = fmaf(__uint_as_float(v[t]), sc, acc[c * kLd + t]);
               acc[c * kLd + t + 1] = fmaf(__uint_as_float(v[t + 1]), sc, acc[c * kLd + t + 1]);
@@ -1553,18 +1584,19 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 constexpr int kMaxDevices = 64;
 
 // weight tiles 64, 128, 256 x (single CTA, CTA pair) + swapped 16/32/64-token
-// tiles + the persistent single-CTA kernel for weight tiles 64, 128, 256
-constexpr int kVariants = 12;
+// tiles + the persistent single-CTA kernel for weight tiles 64, 128, 256, 224
+constexpr int kVariants = 13;
 
 static int variant(int tm, int bn) {
   if (tm < kTileM) return 6 + (tm == 16 ? 0 : tm == 32 ? 1 : 2);
   return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0);
 }
-static int persistent_variant(int bn) { return 9 + (bn == 64 ? 0 : bn == 128 ? 1 : 2); }
+static int persistent_variant(int bn) { return 9 + (bn == 64 ? 0 : bn == 128 ? 1 : bn == 256 ? 2 : 3); }
 
 // Unsplit 128-token plans with more tiles than SMs run on the persistent
 // kernel; FACK_PERSISTENT=0 in the environment keeps them on the one-tile
-// kernel (the two give bitwise identical results).
+// kernel (the two give bitwise identical results).  224-wide weight tiles
+// exist only in the persistent kernel and always run there.
 static bool persistent_enabled() {
   static const bool on = [] {
     const char* e = getenv("FACK_PERSISTENT");
@@ -1657,7 +1689,8 @@ static const KernelEntry& kernel_by_variant(int v) {
       entry<64, false>(),       entry<128, false>(),       entry<256, false>(),
       entry<64, true>(),        entry<128, true>(),        entry<256, true>(),
       swap_entry<16>(),         swap_entry<32>(),          swap_entry<64>(),
-      persistent_entry<64>(),   persistent_entry<128>(),   persistent_entry<256>()};
+      persistent_entry<64>(),   persistent_entry<128>(),   persistent_entry<256>(),
+      persistent_entry<224>()};
   return table[v];
 }
 
@@ -1784,7 +1817,7 @@ static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int 
   const int rows = M < kTileM ? M : kTileM;                          // valid tokens of a full CTA tile
   const double wrows = tm == 256 ? bn / 2.0 : bn;
   const double ingest = (kTileM * 128.0 + wrows * 128.0) / 44.0;
-  const double handshake = bn >= 256 ? 880.0 : bn >= 128 ? 550.0 : 500.0;
+  const double handshake = bn >= 224 ? 880.0 : bn >= 128 ? 550.0 : 500.0;
   const double t_kb = fmax(fmax(ingest, 2.0 * bn), handshake);
   const double out = sp > 1 ? rows * bn * 4.0 * (sp - 1) / sp / 18.0 + 2500.0 : rows * bn * 2.0 / 24.0;
   const double cyc = static_cast<double>(waves) * (steps * t_kb + 4000.0 + out);
@@ -1927,7 +1960,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   if (gy > 65535 || gz > 65535) return fail(FACK_ERR_BAD_SHAPE, "problem too large for one launch (grid y > 65535)");
   // more unsplit single-CTA tiles than SMs: one persistent CTA per SM
   const int64_t tiles = static_cast<int64_t>(gx) * gy;
-  const bool persistent = tm == kTileM && p.split == 1 && persistent_enabled() && tiles > d->sms;
+  const bool persistent = tm == kTileM && p.split == 1 && (bn == 224 || (persistent_enabled() && tiles > d->sms));
   const int v = persistent ? persistent_variant(bn) : variant(tm, bn);
   const int st = ensure_variant(d, v);
   if (st != FACK_OK) return st;
@@ -1937,7 +1970,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   q.tail_split = 0;
   bool fixup = false;
   if (persistent) {
-    gx = d->sms;
+    gx = tiles < d->sms ? static_cast<int>(tiles) : d->sms;
     gy = 1;
     gz = 1;
     int rem = 0, S = 0;
@@ -1989,7 +2022,7 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   fc.stream = stream;
   fc.attrs = nullptr;
   fc.numAttrs = 0;
-  const void* ffn = bn == 64 ? fixup_fn<64>() : bn == 128 ? fixup_fn<128>() : fixup_fn<256>();
+  const void* ffn = bn == 64 ? fixup_fn<64>() : bn == 128 ? fixup_fn<128>() : bn == 224 ? fixup_fn<224>() : fixup_fn<256>();
   void* fargs[] = {&f, &chunks};
   e = cudaLaunchKernelExC(&fc, ffn, fargs);
   if (e != cudaSuccess) return fail(FACK_ERR_LAUNCH, "cudaLaunchKernelExC (tail fix-up)", e);
@@ -2064,9 +2097,17 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
     if (M > tile_m_request || (tile_n_request && tile_n_request != kBlk)) return FACK_ERR_BAD_ARG;
     if (split_k_request && (KB + split_k_request - 1) / split_k_request > kSwapMaxKb) return FACK_ERR_BAD_ARG;
   }
-  if (tile_n_request != 0 && tile_n_request != 64 && tile_n_request != 128 && tile_n_request != 256)
+  if (tile_n_request != 0 && tile_n_request != 64 && tile_n_request != 128 && tile_n_request != 224 &&
+      tile_n_request != 256)
     return FACK_ERR_BAD_ARG;
   if (tile_n_request && N % tile_n_request) return FACK_ERR_BAD_ARG;
+  // 224-wide weight tiles: single 128-token CTAs, one K slice (the persistent kernel only)
+  if (tile_n_request == 224 && ((tile_m_request && tile_m_request != kTileM) || split_k_request > 1))
+    return FACK_ERR_BAD_ARG;
+  if (tile_n_request == 224) {
+    tile_m_request = kTileM;
+    split_k_request = 1;
+  }
   if (tile_m_request == 256 && split_k_request * 2 > kMaxSplit) return FACK_ERR_BAD_ARG;  // cluster of 2 x split
   int tm = tile_m_request, bn = tile_n_request, sp = split_k_request;
   if (sp) {
@@ -2196,7 +2237,8 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
 
   CUtensorMap tw, tx;
   if (wq_packed == FACK_W_PACKED)
-    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk, wrows < kBlk ? wrows : kBlk,
+    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk,
+                   wrows == 224 ? 32 : wrows < kBlk ? wrows : kBlk,   // 224-row tiles: seven 32-row boxes
                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);  // packed tiles are contiguous
   else
     st = encode_2d(&tw, wq, K, N, K, kBlk, wrows, CU_TENSOR_MAP_SWIZZLE_128B);

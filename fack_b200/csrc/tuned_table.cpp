@@ -14,7 +14,7 @@
 // lines are comments; the first other line is a header; columns are found by
 // name, so order and extra columns do not matter.  Required: cu_num, M, N, K,
 // kernelName -- for the FP8 table this library's
-// fack_bs_sm100_t{16|32|64|128|256}x{64|128|256}_s{S}, for the sibling table
+// fack_bs_sm100_t{16|32|64|128|256}x{64|128|224|256}_s{S}, for the sibling table
 // fack_tn_sm100_{bf16|i8}_t{128|256}x{64|128|256}_s{S} (the name gives the
 // family).  Optional: splitK (must equal the name's S) and errRatio (must be
 // 0).  Rows naming another kernel family (a gfx942 symbol, or the other table's
@@ -257,7 +257,8 @@ int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
     return FACK_OK;
   }
   if (tile_m != 128 && tile_m != 256) return FACK_ERR_BAD_ARG;
-  if ((tile_n != 64 && tile_n != 128 && tile_n != 256) || N % tile_n) return FACK_ERR_BAD_ARG;
+  if ((tile_n != 64 && tile_n != 128 && tile_n != 224 && tile_n != 256) || N % tile_n) return FACK_ERR_BAD_ARG;
+  if (tile_n == 224 && (tile_m != 128 || split_k != 1)) return FACK_ERR_BAD_ARG;  // persistent kernel only
   if (split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128) return FACK_ERR_BAD_ARG;
   if (tile_m == 256 && 2 * split_k > kTunedMaxSplit) return FACK_ERR_BAD_ARG;
   return FACK_OK;

@@ -91,8 +91,9 @@ def parse_kernel_name(name) -> tuple:
     applies here, so they (and None / "") leave the choice to the library."""
     if not name or name in AITER_SYMBOLS:
         return 0, 0, 0
-    m = re.fullmatch(KERNEL_PREFIX + r"_t(16|32|64|128|256)x(64|128|256)_s([1-8])", str(name))
-    if not m or (m.group(1) == "256" and int(m.group(3)) > 4) or (int(m.group(1)) < 128 and m.group(2) != "128"):
+    m = re.fullmatch(KERNEL_PREFIX + r"_t(16|32|64|128|256)x(64|128|224|256)_s([1-8])", str(name))
+    if not m or (m.group(1) == "256" and int(m.group(3)) > 4) or (int(m.group(1)) < 128 and m.group(2) != "128") \
+            or (m.group(2) == "224" and (m.group(1) != "128" or m.group(3) != "1")):
         raise ValueError(f"unknown blockscale kernel {name!r}")
     return int(m.group(1)), int(m.group(2)), int(m.group(3))
 
@@ -311,7 +312,8 @@ def gemm_a8w8_blockscale_bpreshuffle_asm(a, b, out, x_scale, w_scale, bias=None,
     accepted and unused.  ``kernelName`` may be None, one of the reviewed
     gfx942 symbols (library choice of tile) or one of this library's names
     ``fack_bs_sm100_t{128|256}x{64|128|256}_s{S}`` (token tile 256 = a CTA
-    pair, S <= 4 then; else S <= 8), which fixes the tiles (and the split,
+    pair, S <= 4 then; else S <= 8) or ``fack_bs_sm100_t128x224_s1`` (224-wide
+    weight tiles, persistent kernel only), which fixes the tiles (and the split,
     unless ``splitK`` is given); ``splitK`` None/0 otherwise lets the library
     choose.  ``bpreshuffle=True`` requires ``b`` from
     :func:`shuffle_weight`.

@@ -89,8 +89,11 @@ const char* fack_last_error(void);
  * for M <= the tile: 128 weight rows on the MMA's M side x all M tokens on its
  * N side, weight tile 128, at most 128 K blocks per slice, split-K always
  * through distributed shared memory, no workspace), the weight-tile width
- * (64, 128 or 256), split-K (1..8; 2 x split <= 8 for pairs) -- 0 for any of them = the
- * library's choice -- and the workspace bytes fack_gemm_bs_ex needs for that
+ * (64, 128, 224 or 256), split-K (1..8; 2 x split <= 8 for pairs) -- 0 for any of them = the
+ * library's choice; a 224-wide weight tile (four per 896 columns: one rank's
+ * shard of a 7168-wide layer over 8 GPUs) is valid with 128-token tiles and
+ * one K slice only, runs on the persistent kernel, and is chosen by request
+ * or by a tuned-table row, never by the cost model -- and the workspace bytes fack_gemm_bs_ex needs for that
  * plan when the caller supplies a workspace (0 for a single K slice).  A
  * library choice of split-K queries the current device (cluster occupancy); an
  * explicit split does not.  When all three requests are 0, an exact-shape row

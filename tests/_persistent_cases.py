@@ -27,3 +27,11 @@ def grouped_tile(lin, n_tiles, m_tiles, group=16):
     gm = min(group, m_tiles - first)
     r = lin - g * per_group
     return first + r % gm, r // gm
+
+# 224-wide tiles (persistent kernel only): no one-tile kernel to compare bit
+# for bit; checked against the fp64 reference and the oracle instead
+CASES_224 = {
+    "t224_shard": (1024, 896, 2048, 224),      # 8 x 4 = 32 tiles (< SMs): one round; packed rows cross tiles
+    "t224_tail": (1280, 3584, 2048, 224),      # 10 x 16 = 160 tiles: tail 12 tiles split 8 ways
+    "t224_ragged": (1000, 7168, 1024, 224),    # 8 x 32 = 256 tiles, last token tile 104 rows; tail 108: no split
+}

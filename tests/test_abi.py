@@ -81,6 +81,12 @@ def test_explicit_split_plan_and_workspace_without_device():
     assert plan(256, 3072, 7168, m=256, s=5)[0] == _lib.FACK_ERR_BAD_ARG
     assert plan(256, 3072, 7168, m=64, s=1)[0] == _lib.FACK_ERR_BAD_ARG
     assert plan(256, 384, 7168, n=256, s=1)[0] == _lib.FACK_ERR_BAD_ARG
+    # 224-wide weight tiles: 128-token tiles and one K slice, filled in when not given (no device query)
+    assert plan(8192, 896, 16384, n=224) == (0, 128, 224, 1, 0)
+    assert plan(8192, 896, 16384, m=128, n=224, s=1) == (0, 128, 224, 1, 0)
+    assert plan(8192, 896, 16384, n=224, s=2)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8192, 896, 16384, m=256, n=224)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8192, 1024, 16384, n=224)[0] == _lib.FACK_ERR_BAD_ARG
     tn2, sk2 = ctypes.c_int(), ctypes.c_int()
     assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tn2), ctypes.byref(sk2)) == 0
     assert (tn2.value, sk2.value) == (256, 6)

@@ -14,7 +14,7 @@ def entry(name, regs, spill_st=0, spill_ld=0):
 
 
 SPLIT = ([f"_ZN4fack14gemm_bs_kernelILi{bn}ELb{p}EEEv14CUtensorMap_st" for bn in (64, 128, 256) for p in (0, 1)] +
-         [f"_ZN4fack25gemm_bs_persistent_kernelILi{bn}EEEv14CUtensorMap_st" for bn in (64, 128, 256)])
+         [f"_ZN4fack25gemm_bs_persistent_kernelILi{bn}EEEv14CUtensorMap_st" for bn in (64, 128, 224, 256)])
 
 
 def clean():

@@ -142,3 +142,13 @@ def test_case_bench_cli_without_a_device():
     if torch.cuda.is_available():
         return
     assert case_bench.main(["256", "3072", "7168", "--plan", "128,256,5"]) == 2
+
+
+def test_kernel_names_with_224_wide_tiles():
+    """fack_bs_sm100_t128x224_s1 names the persistent 224-wide plan; other
+    token tiles or splits with 224 are not plans."""
+    from fack_b200 import ops
+    assert ops.parse_kernel_name("fack_bs_sm100_t128x224_s1") == (128, 224, 1)
+    for bad in ("fack_bs_sm100_t128x224_s2", "fack_bs_sm100_t256x224_s1", "fack_bs_sm100_t64x224_s1"):
+        with pytest.raises(ValueError):
+            ops.parse_kernel_name(bad)

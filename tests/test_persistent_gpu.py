@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import fack_b200 as fb
-from _persistent_cases import CASES, grouped_tile, inputs
+from _persistent_cases import CASES, CASES_224, grouped_tile, inputs
 from oracle.blockscale import reference_gemm
 from test_gemm_gpu import _device_reference, assert_close
 
@@ -34,7 +34,7 @@ def one_tile_outputs(tmp_path_factory, cuda_device):
 
 
 def run(case, dev, tail):
-    M, N, K, tn = CASES[case]
+    M, N, K, tn = {**CASES, **CASES_224}[case]
     xq, xs, wq, ws = inputs(M, N, K, dev)
     out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
     fb.gemm_blockscale(xq, fb.shuffle_weight(wq), xs, ws, out=out, tile_n=tn, tile_m=128, split_k=1, tail=tail)
@@ -83,4 +83,29 @@ def test_tail_split(cuda_device, name):
             mt, nt = grouped_tile(lin, n_tiles, m_tiles)
             tail_mask[mt * 128:(mt + 1) * 128, nt * tn:(nt + 1) * tn] = True
         assert not (diff & ~tail_mask).any(), "a tile outside the tail changed with the tail split"
+    assert fb.device_status() == 0
+
+
+@pytest.mark.parametrize("name", list(CASES_224))
+@pytest.mark.parametrize("packed", [True, False])
+def test_224_wide_tiles(cuda_device, name, packed):
+    """The 224-wide weight tile (four per 896 columns), packed weights in 32-row
+    boxes and row-major in one box; a thread's 112 columns may take two
+    w_scale blocks.  Every element against the fp64 reference, sampled rows
+    against the oracle, the tail split bitwise reproducible."""
+    M, N, K, tn = CASES_224[name]
+    xq, xs, wq, ws = inputs(M, N, K, cuda_device)
+    b = fb.shuffle_weight(wq) if packed else wq
+    ys = []
+    for _ in range(2):
+        out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+        fb.gemm_blockscale(xq, b, xs, ws, out=out, tile_n=224, tile_m=128, split_k=1)
+        torch.cuda.synchronize()
+        ys.append(out)
+    assert torch.isfinite(ys[0].float()).all(), "unwritten output elements"
+    assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16))
+    assert_close(ys[0], _device_reference(xq, xs, wq, ws), name + " 224")
+    rows = torch.linspace(0, M - 1, 12).long()
+    assert_close(ys[0][rows.to(cuda_device)], reference_gemm(xq[rows.to(cuda_device)].cpu(), wq.cpu(),
+                                                             xs[rows.to(cuda_device)].cpu(), ws.cpu()), name)
     assert fb.device_status() == 0

@@ -56,6 +56,9 @@ def test_set_lookup_replace_clear(lib):
     ((148, 0, 3072, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),
     ((148, 256, 3000, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),
     ((148, 65535 * 128 + 1, 3072, 7168, 128, 256, 1), _lib.FACK_ERR_BAD_SHAPE),   # beyond 65535 token tiles
+    ((148, 8192, 896, 16384, 128, 224, 2), _lib.FACK_ERR_BAD_ARG),  # 224-wide tiles: one K slice only
+    ((148, 8192, 896, 16384, 256, 224, 1), _lib.FACK_ERR_BAD_ARG),  # 224-wide tiles: single CTAs only
+    ((148, 8192, 1024, 16384, 128, 224, 1), _lib.FACK_ERR_BAD_ARG),  # 224 does not divide 1024
 ])
 def test_invalid_rows_refused(lib, row, status):
     assert lib.fack_gemm_bs_tuned_set(*row) == status
@@ -135,7 +138,7 @@ def test_tuner_candidates_are_exactly_the_valid_plans():
     lib = _lib.load()
     tm, tn, sk, nb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
     for M, N, K in ((256, 3072, 7168), (48, 4096, 2048), (33, 384, 640), (1, 128, 256), (16, 3072, 7168),
-                    (64, 1024, 40960)):
+                    (64, 1024, 40960), (8192, 896, 16384), (300, 1792, 1024)):
         cands = tune.candidates(M, N, K)
         assert len(set(cands)) == len(cands)
         for c in cands:
@@ -143,7 +146,7 @@ def test_tuner_candidates_are_exactly_the_valid_plans():
                                          ctypes.byref(nb)) == 0
             assert (tm.value, tn.value, sk.value) == c
         for t_m in (16, 32, 64, 128, 256):
-            for t_n in (64, 128, 256):
+            for t_n in (64, 128, 224, 256):
                 for s in range(1, 9):
                     ok = lib.fack_gemm_bs_plan(M, N, K, t_m, t_n, s, ctypes.byref(tm), ctypes.byref(tn),
                                                ctypes.byref(sk), ctypes.byref(nb)) == 0
