@@ -183,16 +183,26 @@ __device__ __noinline__ void xchg_signal_and_wait(XchgState* x, unsigned long lo
   }
 }
 
-// End of a GEMM launch with peer stores (all threads of each CTA): every
-// thread's stores are made visible system-wide, the CTA counts itself in, and
-// the last CTA of the grid runs the exchange step (the classic last-block
-// pattern: fence, then an atomic ticket).  The grid therefore completes only
-// once every rank's blocks have landed in this rank's output, so no separate
-// barrier or collective is needed on the stream.
+// After a thread's peer stores.  Without the fused exchange each storing
+// thread makes its stores visible system-wide itself.  With it, xchg_complete
+// fences once per CTA behind a CTA barrier instead: a fence is cumulative over
+// the stores that the barrier orders before it, and hundreds of per-thread
+// system fences, each waiting on NVLink write acknowledgements, cost more than
+// the stores they follow.
+__device__ __forceinline__ void peer_store_fence(const Params& p) {
+  if (p.n_peer && !p.xchg) __threadfence_system();
+}
+
+// End of a GEMM launch with peer stores (all threads of each CTA): the CTA's
+// stores are made visible system-wide (barrier, then one system fence), the
+// CTA counts itself in, and the last CTA of the grid runs the exchange step
+// (the classic last-block pattern: fence, then an atomic ticket).  The grid
+// therefore completes only once every rank's blocks have landed in this
+// rank's output, so no separate barrier or collective is needed on the stream.
 __device__ __forceinline__ void xchg_complete(const Params& p, unsigned int* status) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
     if (atomicAdd(&p.xchg->arrivals, 1u) == total - 1) {
       __threadfence_system();
@@ -709,7 +719,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const uint4 v = *reinterpret_cast<const uint4*>(stg + r * C::kPitch16 + cc * 8);
         store_out16(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc * 8, v);
       }
-      if (p.n_peer) __threadfence_system();  // peer stores are visible before this grid completes
+      peer_store_fence(p);
       return;
     }
 
@@ -730,7 +740,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       if (ok)
         reduce_dsmem<BN, C::kPitch32>(base + C::kOffA, S, rank0, rank_step, r0, r1, p,
                                       static_cast<int64_t>(m0) * p.ldo + n0);
-      if (p.n_peer) __threadfence_system();
+      peer_store_fence(p);
       cluster_sync_all();
       return;
     }
@@ -748,7 +758,7 @@ gemm_bs_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     if (!ok) return;
     reduce_global<BN, C::kPitch32>(p.partials + tile * S * kTileM * BN, stg32, s, S, r0, r1, p,
                                    static_cast<int64_t>(m0) * p.ldo + n0);
-    if (p.n_peer) __threadfence_system();
+    peer_store_fence(p);
   };
   store_output();
   if (p.xchg) xchg_complete(p, status);
@@ -1271,7 +1281,7 @@ gemm_bs_tail_fixup_kernel(const __grid_constant__ Params p, int chunks) {
     }
     store_out8(p, static_cast<int64_t>(m0 + r) * p.ldo + n0 + cc, pack_bf16x4(sum));
   }
-  if (p.n_peer) __threadfence_system();
+  peer_store_fence(p);
   grid_launch_dependents();
   if (p.xchg) xchg_complete(p, &g_status);
 }
@@ -1502,7 +1512,7 @@ gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
         const float4 v = *reinterpret_cast<const float4*>(stg + t * C::kPitch + c);
         store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(v));
       }
-      if (p.n_peer) __threadfence_system();
+      peer_store_fence(p);
     }
   } else {
     // split-K: every CTA of the cluster reaches both barriers, also after an
@@ -1525,7 +1535,7 @@ gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
         }
         store_out8(p, static_cast<int64_t>(t) * p.ldo + n0 + c, pack_bf16x4(sum));
       }
-      if (p.n_peer) __threadfence_system();
+      peer_store_fence(p);
     }
     cluster_sync_all();
   }
