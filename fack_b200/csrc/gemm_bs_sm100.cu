@@ -121,15 +121,17 @@ constexpr unsigned int kStExchange = 32u;  // a peer's completion signal did not
 
 // Completion state of the fused all-gather, one per rank in that rank's
 // device memory (FACK_XCHG_BYTES, zero before first use), mapped into every
-// other rank.  done[s] is written only by rank s (over NVLink): the number of
-// exchanges rank s has finished, i.e. after which every block rank s stores
-// into this rank's output has landed.
+// other rank.  done[s] is added to only by rank s (over NVLink): each CTA of
+// an exchange launch on rank s adds its share of 2^32 once its stores into
+// this rank's output have landed, the shares of one launch summing to exactly
+// 2^32 whatever its grid size.  So done[s] >= e * 2^32 once rank s's first e
+// exchanges have landed here.
 struct XchgState {
-  unsigned int arrivals;              // CTAs of the current launch that have finished their stores
-  unsigned int reserved;
-  unsigned long long seq;             // exchanges this rank has taken part in
+  unsigned int reserved[2];
+  unsigned long long seq;             // exchanges this rank has completed
   unsigned long long done[kMaxRanks];
 };
+constexpr int kXchgShift = 32;        // one exchange adds 2^32 to each peer's done[rank]
 static_assert(sizeof(XchgState) <= FACK_XCHG_BYTES, "exchange state outgrew FACK_XCHG_BYTES");
 
 struct Params {
@@ -158,22 +160,35 @@ struct Params {
   uint64_t xchg_timeout_ns;
 };
 
-// One exchange step of this rank: tell every peer that this rank's stores
-// into its output have landed (release store of the new step number into
-// done[rank] of each peer's state), then wait until every peer has said the
-// same to this rank (acquire loads of this rank's done[]).  The wait is
-// bounded: on expiry it ORs kStExchange into the status word and returns.
-// One thread; every call on a rank's state comes from one stream, in the same
-// order on every rank, so the step numbers agree.
-__device__ __noinline__ void xchg_signal_and_wait(XchgState* x, unsigned long long* const* peer_done, int n_peer,
-                                                  int rank, int world, uint64_t timeout_ns, unsigned int* status) {
+// This CTA's part of an exchange launch (one thread, after a system fence
+// that covers the CTA's peer stores): add its share of 2^32 to done[rank] of
+// every peer's state.  Relaxed adds: the fence before them is the release.
+__device__ __forceinline__ void xchg_post(unsigned long long* const* peer_done, int n_peer, unsigned int cta,
+                                          unsigned int ctas) {
+  // 2^32 = ctas * q + r + 1 with q, r the quotient and remainder of 2^32 - 1
+  const unsigned int q = 0xffffffffu / ctas, r = 0xffffffffu % ctas;
+  const bool exact = (r + 1u == ctas);
+  const unsigned long long base = static_cast<unsigned long long>(q) + (exact ? 1ull : 0ull);
+  const unsigned int rem = exact ? 0u : r + 1u;
+  const unsigned long long share = base + (cta < rem ? 1ull : 0ull);
+  for (int d = 0; d < n_peer; ++d) red_add_relaxed_sys_u64(peer_done[d], share);
+}
+
+// The wait of one exchange step on this rank (one thread of the launch):
+// until every peer's shares for this step have arrived (acquire loads of this
+// rank's done[]), then count the step.  The wait is bounded: on expiry it ORs
+// kStExchange into the status word and returns.  Every call on a rank's state
+// comes from one stream, in the same order on every rank, so the step numbers
+// agree; a peer already posting its next step only pushes done[] further.
+__device__ __noinline__ void xchg_wait(XchgState* x, int rank, int world, uint64_t timeout_ns,
+                                       unsigned int* status) {
   const unsigned long long seq = x->seq + 1;
   x->seq = seq;
-  for (int d = 0; d < n_peer; ++d) st_release_sys_u64(peer_done[d], seq);
+  const unsigned long long target = seq << kXchgShift;
   const uint64_t t0 = global_timer_ns();
   for (int s = 0; s < world; ++s) {
     if (s == rank) continue;
-    while (ld_acquire_sys_u64(&x->done[s]) < seq) {
+    while (ld_acquire_sys_u64(&x->done[s]) < target) {
       if (global_timer_ns() - t0 > timeout_ns) {
         atomicOr(status, kStExchange);
         return;
@@ -195,21 +210,23 @@ __device__ __forceinline__ void peer_store_fence(const Params& p) {
 
 // End of a GEMM launch with peer stores (all threads of each CTA): the CTA's
 // stores are made visible system-wide (barrier, then one system fence), the
-// CTA counts itself in, and the last CTA of the grid runs the exchange step
-// (the classic last-block pattern: fence, then an atomic ticket).  The grid
+// CTA posts its share to every peer straight away, and CTA 0 waits for every
+// peer's shares.  No CTA waits on another CTA of its own grid (no ticket):
+// the last peer store to land is followed only by one NVLink add.  The grid
 // therefore completes only once every rank's blocks have landed in this
 // rank's output, so no separate barrier or collective is needed on the stream.
+// The posting thread's work is kept out of line so that its registers are
+// allocated apart from the kernels'.
+__device__ __noinline__ void xchg_post_and_wait(const Params& p, unsigned int* status) {
+  const unsigned int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  __threadfence_system();
+  xchg_post(p.peer_done, p.n_peer, cta, gridDim.x * gridDim.y * gridDim.z);
+  if (cta == 0) xchg_wait(p.xchg, p.rank, p.world, p.xchg_timeout_ns, status);
+}
+
 __device__ __forceinline__ void xchg_complete(const Params& p, unsigned int* status) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-    if (atomicAdd(&p.xchg->arrivals, 1u) == total - 1) {
-      __threadfence_system();
-      p.xchg->arrivals = 0;  // every CTA of this launch has counted itself: ready for the next launch
-      xchg_signal_and_wait(p.xchg, p.peer_done, p.n_peer, p.rank, p.world, p.xchg_timeout_ns, status);
-    }
-  }
+  if (threadIdx.x == 0) xchg_post_and_wait(p, status);
 }
 
 __device__ __forceinline__ uint2 pack_bf16x4(const float4& v) {
@@ -1545,8 +1562,11 @@ gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
 // A stand-alone exchange step (one thread): orders a rank's next peer stores
 // after everything its stream did before, on every rank.
 __global__ void xchg_barrier_kernel(XchgState* x, Params pd, uint64_t timeout_ns) {
-  if (threadIdx.x == 0)
-    xchg_signal_and_wait(x, pd.peer_done, pd.n_peer, pd.rank, pd.world, timeout_ns, &g_status);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    xchg_post(pd.peer_done, pd.n_peer, 0, 1);
+    xchg_wait(x, pd.rank, pd.world, timeout_ns, &g_status);
+  }
 }
 
 // ------------------------------------------------------------------ prepack --
