@@ -13,7 +13,7 @@ transposed-contiguous x_scale).  Under torchrun (``--gpus N``) the output
 columns are sharded over the ranks (strong scaling): rank r holds WQ rows
 [r*N/g, (r+1)*N/g), and each step is one launch per rank whose epilogue
 stores every bf16 tile into every rank's Y over NVLink peer mappings and
-whose last CTA completes the exchange on the device (``--gather fused``,
+whose CTAs complete the exchange on the device (``--gather fused``,
 the default), or the blocks are all-gathered over NCCL and interleaved
 (``--gather nccl``).  The decode shape M=256, N=3072, K=7168 is measured
 beside it on every rank (key ``decode``) and can be the headline with
@@ -474,8 +474,9 @@ def run_ours(args):
                          f" (> 126 MB L2)",
                    "timing": f"{timing}, CUDA events on the launch stream, max over ranks",
                    "parallelism": ((f"N-shard g={world}: one launch per rank per step; its epilogue stores every "
-                                    "tile to all ranks' Y over NVLink peer mappings (CUDA IPC) and its last CTA "
-                                    "signals the peers and waits for theirs (no collective on the stream)"
+                                    "tile to all ranks' Y over NVLink peer mappings (CUDA IPC); each CTA counts its "
+                                    "landed stores into every peer's exchange state and CTA 0 waits for the "
+                                    "peers' counts (no collective on the stream)"
                                     if args.gather == "fused" else f"N-shard g={world} + NCCL all-gather")
                                    if sharded else
                                    ("single GPU" if world == 1 else f"{world} independent replicas"))},

@@ -11,9 +11,10 @@ the replicated row-major Y[M, N]:
   column block r of every rank's Y through NVLink peer mappings (CUDA IPC),
   so the exchange overlaps the math tile by tile and no separate gather or
   interleave runs.  The launch orders itself against the other ranks on the
-  device (``fack_gemm_bs_allgather``): its last CTA signals every peer over
-  NVLink and waits, bounded, for every peer's signal, so the call holds no
-  collective and its completion on the stream means Y is whole.
+  device (``fack_gemm_bs_allgather``): each CTA counts its landed stores into
+  every peer's exchange state over NVLink and CTA 0 waits, bounded, for every
+  peer's counts, so the call holds no collective and its completion on the
+  stream means Y is whole.
 * ``mode="nccl"``: the block goes to this rank's slot of a [g, M, N/g] gather
   buffer, an in-place NCCL all-gather fills the other slots, and a
   column-interleave kernel assembles Y (also the gloo path of the CPU tests).

@@ -158,11 +158,12 @@ int fack_gemm_bs_bcast(const void* xq, int64_t ldx, const void* wq, int wq_packe
 
 /*
  * The fused compute + all-gather with its own completion: fack_gemm_bs_bcast
- * to the world - 1 peers (peer_outs, in rank order without `rank`), where the
- * last CTA of the grid to finish then signals every peer that this rank's
- * blocks have landed (a release store over NVLink into that peer's exchange
- * state, peer_xchg[i] in the same order) and waits, bounded by 10 s, until
- * every peer has signalled this rank.  When the launch completes on `stream`,
+ * to the world - 1 peers (peer_outs, in rank order without `rank`), where
+ * each CTA, once its blocks have landed, adds its share of the step to every
+ * peer's exchange state over NVLink (peer_xchg[i] in the same order; the
+ * shares of one launch sum to one step whatever its grid size) and CTA 0
+ * waits, bounded by 10 s, until every peer's shares for this step have
+ * arrived in this rank's state.  When the launch completes on `stream`,
  * this rank's Y holds every rank's block: no barrier or collective is needed
  * around it.  2 <= world <= 8.  On a wait that runs out the device status word
  * gets FACK_DEVICE_EXCHANGE (fack_device_status) and the launch still ends.
