@@ -60,6 +60,8 @@ constexpr int kEpiWarp0 = 4;       // warpgroup 0: TMA, MMA, 2 spare; warps 4..1
 constexpr int kPrefetch = 4;       // K blocks of scales prefetched ahead by cp.async
 constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kSwapMaxKb = 128;    // swapped small-M tiles: K blocks per CTA whose scales fit in shared memory
+constexpr int kSmallRows = 16;     // weight rows per CTA of the warp-MMA small-M kernel (its plans' tile_n)
+constexpr int kSmallMaxKb = 256;   // warp-MMA small-M kernel: K blocks whose scale table fits in shared memory
 constexpr int kGroupM = 16;        // token-tile band of the grouped launch order
 constexpr int kSmemBudget = 196608;
 // Register split (setmaxnreg).  The kernel is launched with kLaunchRegs per
@@ -240,6 +242,10 @@ __device__ __forceinline__ uint2 pack_bf16x4(const float4& v) {
 
 // Element offset `off` of the output: each peer's copy first (the NVLink
 // stores have the longer way to go), then this GPU's.
+__device__ __forceinline__ void store_out4(const Params& p, int64_t off, uint32_t v) {
+  for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint32_t*>(p.peer_out[d] + off) = v;
+  *reinterpret_cast<uint32_t*>(p.out + off) = v;
+}
 __device__ __forceinline__ void store_out8(const Params& p, int64_t off, const uint2& v) {
   for (int d = 0; d < p.n_peer; ++d) *reinterpret_cast<uint2*>(p.peer_out[d] + off) = v;
   *reinterpret_cast<uint2*>(p.out + off) = v;
@@ -1559,6 +1565,179 @@ gemm_bs_swap_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   if (p.xchg) xchg_complete(p, status);
 }
 
+// ------------------------------------------------ small M (warp-level MMA) --
+// For a few tokens the call is the weight stream and its fixed cost, and the
+// tensor-memory pipeline's fixed cost (descriptor fetch, barrier set-up, TMEM
+// allocation, cluster launch and barriers, the split-K combine) is most of
+// it.  This kernel has none of that.  A CTA owns 16 weight rows and all M <= 16
+// tokens; its 8 warps split the K blocks.  Each warp streams its K blocks'
+// 16 x 128 weight bytes and 16 x 128 token bytes through a kStages-deep ring
+// of its own in shared memory (cp.async, 512 contiguous bytes per warp
+// instruction, kStages - 1 K blocks in flight) and feeds them to warp-level
+// MMAs (m16n8k32, e4m3 x e4m3 -> f32), one or two per 32-wide K step (tokens
+// 0-7, 8-15).  Each K block's f32 tile is scaled by
+// w_scale[n/128, kb] * x_scale[t, kb] (a table computed once into shared
+// memory, zero for tokens >= M) and accumulated; the warps' partials are
+// summed in shared memory in warp order (deterministic) and stored as bf16.
+//
+// The ring holds each 128-byte row with its 16-byte chunks swizzled, logical
+// chunk c of row r at c ^ (r & 7) -- the packed weight layout as it is, row-
+// major weights and tokens rearranged on the way in -- so that the fragment
+// reads below are free of bank conflicts.  Operand placement: thread
+// (g = lane/4, q = lane%4) takes logical chunks 2q and 2q+1 of weight rows g
+// and g+8; in K step s (0..3) word s of chunk 2q is the MMA's A column block
+// 4q.. (a0 for row g, a1 for row g+8) and word s of chunk 2q+1 the block
+// 16+4q.. (a2, a3); the token operand takes the same words of the token's
+// chunks 2q and 2q+1 (b0, b1) for token g (and g+8 in the second MMA).  Any
+// one-to-one map of the K block's 128 positions onto the MMA's 4 x 32 gives
+// the same sum as long as both operands share it.
+struct SmallCfg {
+  static constexpr int kThreads = 256;
+  static constexpr int kWarps = kThreads / 32;
+  static constexpr int kRows = 16;                          // weight rows per CTA = tokens at most
+  static constexpr int kStages = 3;                         // ring depth per warp
+  static constexpr int kStageBytes = 2 * kRows * kBlk;      // weights, then tokens: 16 rows x 128 B each
+  static constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+  static constexpr int kPitch = kRows + 1;                  // partials: [warp][row][token], padded rows
+  static constexpr int kMaxKb = kSmallMaxKb;
+  static constexpr int kSmemBytes = kRingBytes + kMaxKb * kRows * 4;   // + the scale table [KB][16]
+  static_assert(kWarps * kRows * kPitch * 4 <= kRingBytes, "partials reuse the ring");
+  static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
+};
+
+__global__ void __launch_bounds__(SmallCfg::kThreads, 2)
+gemm_bs_small_kernel(const uint8_t* __restrict__ xq, int64_t ldx, const uint8_t* __restrict__ wq,
+                     const __grid_constant__ Params p) {
+  using C = SmallCfg;
+  extern __shared__ __align__(128) uint8_t small_smem[];
+  float* scale_tab = reinterpret_cast<float*>(small_smem + C::kRingBytes);   // [KB][16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int n0 = blockIdx.x * C::kRows;
+  const int KB = p.KB;
+  const int kb_begin = (warp * KB) / C::kWarps;
+  const int nk = ((warp + 1) * KB) / C::kWarps - kb_begin;
+  const bool two = p.M > 8;                          // tokens 8-15 take a second MMA
+
+  // Copy side: lane -> row lr + 4k (k = 0..3) and logical-or-stored chunk lc.
+  const int lr = lane >> 3, lc = lane & 7;
+  const uint8_t* wsrc;
+  int64_t w_row_step, w_kb_step;
+  int w_dst_c;                                       // chunk position in the ring; -1: swizzle on the way in
+  if (p.w_packed) {
+    // tile (n0/128, kb) is 128 rows x 128 B, chunks already at c ^ (row & 7);
+    // n0 is a multiple of 16, so a tile row and its CTA row agree mod 8
+    wsrc = wq + static_cast<int64_t>(n0 >> 7) * KB * (kBlk * kBlk) + static_cast<int64_t>((n0 & 127) + lr) * kBlk +
+           lc * 16;
+    w_row_step = 4 * kBlk;
+    w_kb_step = kBlk * kBlk;
+    w_dst_c = lc;
+  } else {
+    wsrc = wq + static_cast<int64_t>(n0 + lr) * p.K + lc * 16;
+    w_row_step = 4 * static_cast<int64_t>(p.K);
+    w_kb_step = kBlk;
+    w_dst_c = -1;                                    // swizzle on the way in
+  }
+  wsrc += static_cast<int64_t>(kb_begin) * w_kb_step;
+  const uint8_t* xsrc = xq + static_cast<int64_t>(kb_begin) * kBlk + lc * 16;
+  const uint32_t ring = smem_addr(small_smem) + warp * (C::kStages * C::kStageBytes);
+  const uint8_t* ring_ptr = small_smem + warp * (C::kStages * C::kStageBytes);
+
+  grid_dependency_wait();
+
+  auto issue = [&](int i) {  // the i-th K block of this warp into stage i % kStages
+    if (i < nk) {
+      const uint32_t wdst = ring + (i % C::kStages) * C::kStageBytes;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = lr + 4 * k;
+        const int pos = w_dst_c >= 0 ? w_dst_c : (lc ^ (r & 7));
+        cp_async16_cg(wdst + r * kBlk + pos * 16, wsrc + static_cast<int64_t>(i) * w_kb_step + k * w_row_step);
+        const uint32_t xdst = wdst + C::kRows * kBlk;
+        const bool tok = r < p.M;
+        const uint8_t* xs = tok ? xsrc + static_cast<int64_t>(r) * ldx + static_cast<int64_t>(i) * kBlk : xsrc;
+        cp_async16_cg_fill(xdst + r * kBlk + (lc ^ (r & 7)) * 16, xs, tok ? 16u : 0u);
+      }
+    }
+    cp_async_commit();  // one group per K block, empty past the end, so the counts below hold
+  };
+#pragma unroll
+  for (int i = 0; i < C::kStages - 1; ++i) issue(i);
+
+  {
+    const float* ws_row = p.w_scale + static_cast<int64_t>(n0 >> 7) * KB;
+    for (int i = threadIdx.x; i < KB * C::kRows; i += C::kThreads) {
+      const int kb = i / C::kRows, t = i - kb * C::kRows;
+      scale_tab[i] = t < p.M ? ws_row[kb] * p.x_scale[t * p.xs_sm + static_cast<int64_t>(kb) * p.xs_sk] : 0.f;
+    }
+  }
+  __syncthreads();  // the scale table is whole
+
+  // fragment side: this thread's chunks 2q, 2q+1 of row g (and g+8, which
+  // shares g & 7) sit at byte offsets o_lo, o_hi of a row
+  const int o_lo = ((2 * q) ^ (g & 7)) * 16, o_hi = ((2 * q + 1) ^ (g & 7)) * 16;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int i = 0; i < nk; ++i) {
+    __syncwarp();                                    // every lane has read the stage refilled next
+    issue(i + C::kStages - 1);
+    cp_async_wait<C::kStages - 1>();                 // this lane's copies of K block i have landed ...
+    __syncwarp();                                    // ... and every other lane's
+    const uint8_t* w = ring_ptr + (i % C::kStages) * C::kStageBytes;
+    const uint8_t* x = w + C::kRows * kBlk;         // the tokens' rows (zeros past M)
+    const uint4 wa0 = *reinterpret_cast<const uint4*>(w + g * kBlk + o_lo);
+    const uint4 wa1 = *reinterpret_cast<const uint4*>(w + g * kBlk + o_hi);
+    const uint4 wb0 = *reinterpret_cast<const uint4*>(w + (g + 8) * kBlk + o_lo);
+    const uint4 wb1 = *reinterpret_cast<const uint4*>(w + (g + 8) * kBlk + o_hi);
+    const int kb = kb_begin + i;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j == 1 && !two) break;
+      const uint4 x0 = *reinterpret_cast<const uint4*>(x + (8 * j + g) * kBlk + o_lo);
+      const uint4 x1 = *reinterpret_cast<const uint4*>(x + (8 * j + g) * kBlk + o_hi);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_e4m3_m16n8k32(d, wa0.x, wb0.x, wa1.x, wb1.x, x0.x, x1.x);
+      mma_e4m3_m16n8k32(d, wa0.y, wb0.y, wa1.y, wb1.y, x0.y, x1.y);
+      mma_e4m3_m16n8k32(d, wa0.z, wb0.z, wa1.z, wb1.z, x0.z, x1.z);
+      mma_e4m3_m16n8k32(d, wa0.w, wb0.w, wa1.w, wb1.w, x0.w, x1.w);
+      // d0, d1: row g, tokens 8j+2q, 8j+2q+1; d2, d3: row g+8, the same tokens
+      const float2 sc = *reinterpret_cast<const float2*>(scale_tab + kb * C::kRows + 8 * j + 2 * q);
+      acc[j][0] = fmaf(d[0], sc.x, acc[j][0]);
+      acc[j][1] = fmaf(d[1], sc.y, acc[j][1]);
+      acc[j][2] = fmaf(d[2], sc.x, acc[j][2]);
+      acc[j][3] = fmaf(d[3], sc.y, acc[j][3]);
+    }
+  }
+  cp_async_wait<0>();
+  grid_launch_dependents();
+
+  __syncthreads();  // every warp is done with the ring, which now holds the partials
+  float* red = reinterpret_cast<float*>(small_smem);  // [warp][row * kPitch + token]
+  float* mine = red + warp * (C::kRows * C::kPitch);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int t0 = 8 * j + 2 * q;
+    mine[g * C::kPitch + t0] = acc[j][0];
+    mine[g * C::kPitch + t0 + 1] = acc[j][1];
+    mine[(g + 8) * C::kPitch + t0] = acc[j][2];
+    mine[(g + 8) * C::kPitch + t0 + 1] = acc[j][3];
+  }
+  __syncthreads();
+  // thread -> (token t, rows r, r+1): 8 threads cover a token's 16 rows
+  const int t = threadIdx.x >> 3, r = (threadIdx.x & 7) * 2;
+  if (t < p.M && t < C::kRows) {
+    float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < C::kWarps; ++w) {
+      y0 += red[w * (C::kRows * C::kPitch) + r * C::kPitch + t];
+      y1 += red[w * (C::kRows * C::kPitch) + (r + 1) * C::kPitch + t];
+    }
+    const __nv_bfloat162 b = __floats2bfloat162_rn(y0, y1);
+    store_out4(p, static_cast<int64_t>(t) * p.ldo + n0 + r, *reinterpret_cast<const uint32_t*>(&b));
+  }
+  peer_store_fence(p);
+  if (p.xchg) xchg_complete(p, &g_status);
+}
+
 // A stand-alone exchange step (one thread): orders a rank's next peer stores
 // after everything its stream did before, on every rank.
 __global__ void xchg_barrier_kernel(XchgState* x, Params pd, uint64_t timeout_ns) {
@@ -1615,9 +1794,11 @@ constexpr int kMaxDevices = 64;
 
 // weight tiles 64, 128, 256 x (single CTA, CTA pair) + swapped 16/32/64-token
 // tiles + the persistent single-CTA kernel for weight tiles 64, 128, 256, 224
-constexpr int kVariants = 13;
+// + the warp-MMA small-M kernel for up to 16 tokens (16-row weight tiles)
+constexpr int kVariants = 14;
 
 static int variant(int tm, int bn) {
+  if (bn == kSmallRows) return 13;
   if (tm < kTileM) return 6 + (tm == 16 ? 0 : tm == 32 ? 1 : 2);
   return (bn == 64 ? 0 : bn == 128 ? 1 : 2) + (tm == 256 ? 3 : 0);
 }
@@ -1714,13 +1895,17 @@ static KernelEntry persistent_entry() {
   return {reinterpret_cast<const void*>(gemm_bs_persistent_kernel<BN>), PCfg<BN>::kSmemBytes, kThreads, true};
 }
 
+static KernelEntry small_entry() {
+  return {reinterpret_cast<const void*>(gemm_bs_small_kernel), SmallCfg::kSmemBytes, SmallCfg::kThreads, false};
+}
+
 static const KernelEntry& kernel_by_variant(int v) {
   static const KernelEntry table[kVariants] = {
       entry<64, false>(),       entry<128, false>(),       entry<256, false>(),
       entry<64, true>(),        entry<128, true>(),        entry<256, true>(),
       swap_entry<16>(),         swap_entry<32>(),          swap_entry<64>(),
       persistent_entry<64>(),   persistent_entry<128>(),   persistent_entry<256>(),
-      persistent_entry<224>()};
+      persistent_entry<224>(),  small_entry()};
   return table[v];
 }
 
@@ -1789,6 +1974,12 @@ static int co_resident(DeviceInfo* d, int tm, int bn, int split) {
 // valid token) so that the pair lies along the cluster's x dimension,
 // y = weight tiles.  z = K slices.
 static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, int* gz) {
+  if (bn == kSmallRows) {  // warp-MMA small-M kernel: x = 16-row weight tiles, K split inside the CTA
+    *gx = N / kSmallRows;
+    *gy = 1;
+    *gz = 1;
+    return;
+  }
   if (tm < kTileM) {  // swapped small-M tiles: x = 128-row weight tiles
     *gx = N / kBlk;
     *gy = 1;
@@ -1821,6 +2012,15 @@ static void plan_grid(int M, int N, int tm, int bn, int sp, int* gx, int* gy, in
 // time of the operands.
 static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int sp) {
   const int KB = K / kBlk;
+  if (bn == kSmallRows) {
+    // warp-MMA small-M kernel: the weight stream at HBM speed, plus the
+    // first loads' latency and exit; no pipeline to fill, no split-K combine
+    (void)d;
+    (void)sp;
+    (void)KB;
+    const double bytes = static_cast<double>(N) * K + static_cast<double>(M) * K;
+    return bytes / 6.5e12 * 1.9e9 + 2500.0;
+  }
   if (tm < kTileM) {
     // swapped small-M tiles: 128 weight rows x tm tokens; eight TMEM buffers
     // hide the rescale, so a K block costs the fill (weight tile + token
@@ -1860,9 +2060,9 @@ static double plan_cost(DeviceInfo* d, int M, int N, int K, int tm, int bn, int 
 // token tiles unless pairs are requested, then the largest weight tile that
 // still gives >= 120 CTAs, else the smallest.
 static void tiles_for_split(int M, int N, int sp, int tm_req, int bn_req, int* tm, int* bn) {
-  if (tm_req && tm_req < kTileM) {  // swapped small-M tiles always span 128 weight rows
+  if (tm_req && tm_req < kTileM) {  // swapped small-M tiles span 128 weight rows, the warp-MMA ones 16
     *tm = tm_req;
-    *bn = kBlk;
+    *bn = bn_req == kSmallRows ? kSmallRows : kBlk;
     return;
   }
   int t = tm_req ? tm_req : 128;
@@ -1897,6 +2097,18 @@ static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req,
   // swapped small-M tiles: the requested one, else the smallest token tile
   // that holds all M tokens
   const int tm_swap = tm_req && tm_req < kTileM ? tm_req : tm_req ? 0 : M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
+  // the warp-MMA small-M kernel for up to 8 tokens (only when no tile is
+  // requested: a requested 16-token tile alone means the swapped kernel).
+  // Paired A/B at N=3072, K=7168 against the swapped kernel's 16 x 128 split-5
+  // plan: 1.07-1.10x at M=1, 1.07x at M=8, even at M=4, 0.93x at M=16 (its
+  // second token group doubles the MMAs and the token bytes per K block).
+  if (!tm_req && !bn_req && M <= 8 && KB <= kSmallMaxKb) {
+    const int tm_small = 16;
+    best = plan_cost(d, M, N, K, tm_small, kSmallRows, 1);
+    bt = tm_small;
+    bb = kSmallRows;
+    bs = 1;
+  }
   if (tm_swap && M <= tm_swap && (bn_req == 0 || bn_req == kBlk)) {
     for (int sp = 1; sp <= KB && sp <= kMaxSplit; ++sp) {
       if ((KB + sp - 1) / sp > kSwapMaxKb) continue;
@@ -1935,7 +2147,7 @@ static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req,
 }
 
 static size_t workspace_bytes_for(int M, int N, int tm, int bn, int split) {
-  if (split <= 1 || tm < kTileM) return 0;  // swapped tiles combine through distributed shared memory only
+  if (split <= 1 || tm < kTileM) return 0;  // small-M plans combine on chip only
   int gx, gy, gz;
   plan_grid(M, N, tm, bn, split, &gx, &gy, &gz);
   return static_cast<size_t>(gx) * gy * split * kTileM * bn * sizeof(float);
@@ -2059,6 +2271,31 @@ static int launch(DeviceInfo* d, int tm, int bn, const CUtensorMap& tw, const CU
   return FACK_OK;
 }
 
+// The warp-MMA small-M kernel: one CTA per 16 weight rows, plain
+// pointers instead of tensor maps, no cluster.
+static int launch_small(DeviceInfo* d, int tm, const uint8_t* xq, int64_t ldx, const uint8_t* wq, const Params& p,
+                        cudaStream_t stream) {
+  const int v = variant(tm, kSmallRows);
+  const int st = ensure_variant(d, v);
+  if (st != FACK_OK) return st;
+  const KernelEntry& k = kernel_by_variant(v);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.N / kSmallRows, 1, 1);
+  cfg.blockDim = dim3(k.threads, 1, 1);
+  // the cp.async ring and the scale table of this launch's K blocks
+  cfg.dynamicSmemBytes = SmallCfg::kRingBytes + static_cast<size_t>(p.KB) * kSmallRows * sizeof(float);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Params q = p;
+  void* args[] = {const_cast<uint8_t**>(&xq), &ldx, const_cast<uint8_t**>(&wq), &q};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, k.fn, args);
+  return e == cudaSuccess ? FACK_OK : fail(FACK_ERR_LAUNCH, "cudaLaunchKernelExC (small M)", e);
+}
+
 // ------------------------------------------------------ no-alloc scratch --
 // Split-K scratch for fack_gemm_bs_noalloc: part of the library's own device
 // image, so it exists on every GPU that loads the library, from load until the
@@ -2123,6 +2360,17 @@ int fack_gemm_bs_plan(int M, int N, int K, int tile_m_request, int tile_n_reques
   if (tile_m_request != 0 && tile_m_request != 16 && tile_m_request != 32 && tile_m_request != 64 &&
       tile_m_request != 128 && tile_m_request != 256)
     return FACK_ERR_BAD_ARG;
+  if (tile_n_request == kSmallRows) {
+    // the warp-MMA small-M kernel: up to 16 tokens, K split inside the CTA
+    if (tile_m_request != 0 && tile_m_request != 16) return FACK_ERR_BAD_ARG;
+    const int tm = 16;
+    if (M > tm || split_k_request > 1 || KB > kSmallMaxKb) return FACK_ERR_BAD_ARG;
+    *tile_m = tm;
+    *tile_n = kSmallRows;
+    *split_k = 1;
+    if (workspace_bytes) *workspace_bytes = 0;
+    return FACK_OK;
+  }
   if (tile_m_request && tile_m_request < kTileM) {  // swapped small-M tiles
     if (M > tile_m_request || (tile_n_request && tile_n_request != kBlk)) return FACK_ERR_BAD_ARG;
     if (split_k_request && (KB + split_k_request - 1) / split_k_request > kSwapMaxKb) return FACK_ERR_BAD_ARG;
@@ -2265,17 +2513,6 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   if (need && workspace && (workspace_bytes < need || !aligned(workspace, 16))) return FACK_ERR_WS_TOO_SMALL;
   if (!workspace) workspace_bytes = 0;
 
-  CUtensorMap tw, tx;
-  if (wq_packed == FACK_W_PACKED)
-    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk,
-                   wrows == 224 ? 32 : wrows < kBlk ? wrows : kBlk,   // 224-row tiles: seven 32-row boxes
-                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);  // packed tiles are contiguous
-  else
-    st = encode_2d(&tw, wq, K, N, K, kBlk, wrows, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != FACK_OK) return st;
-  st = encode_2d(&tx, xq, K, M, ldx, kBlk, tm < kTileM ? tm : kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != FACK_OK) return st;
-
   Params p;
   p.x_scale = x_scale;
   p.xs_sm = xs_stride_m;
@@ -2310,6 +2547,20 @@ static int gemm_bs_impl(const void* xq, int64_t ldx, const void* wq, int wq_pack
   p.tail_rem = 0;
   p.tail_split = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bn == kSmallRows) return launch_small(d, tm, static_cast<const uint8_t*>(xq), ldx,
+                                            static_cast<const uint8_t*>(wq), p, s);
+
+  CUtensorMap tw, tx;
+  if (wq_packed == FACK_W_PACKED)
+    st = encode_2d(&tw, wq, kBlk, static_cast<uint64_t>(N) * KB, kBlk, kBlk,
+                   wrows == 224 ? 32 : wrows < kBlk ? wrows : kBlk,   // 224-row tiles: seven 32-row boxes
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);  // packed tiles are contiguous
+  else
+    st = encode_2d(&tw, wq, K, N, K, kBlk, wrows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != FACK_OK) return st;
+  st = encode_2d(&tx, xq, K, M, ldx, kBlk, tm < kTileM ? tm : kTileM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != FACK_OK) return st;
+
   return launch(d, tm, bn, tw, tx, p, M, s, workspace ? workspace_bytes : 0);
 }
 

@@ -349,6 +349,14 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
                : "memory");
 }
+// 16-byte asynchronous global->shared copy through L2 only (data read once)
+__device__ __forceinline__ void cp_async16_cg(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// the same, reading src_bytes (0 or 16) and zero-filling the rest
+__device__ __forceinline__ void cp_async16_cg_fill(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -496,6 +504,20 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// Warp-level MMA, D (16x8 f32) += A (16x32 e4m3, row) * B (32x8 e4m3, col).
+// Fragments (g = lane / 4, q = lane % 4): a0 / a1 hold A rows g / g+8 at
+// columns 4q..4q+3, a2 / a3 the same rows at columns 16+4q..; b0 / b1 hold B
+// column g at rows 4q.. / 16+4q..; d0, d1 are D row g at columns 2q, 2q+1 and
+// d2, d3 row g+8 at the same columns.
+__device__ __forceinline__ void mma_e4m3_m16n8k32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                  uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // relaxed system-scope add (no return value); a preceding fence makes it a release
 __device__ __forceinline__ void red_add_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

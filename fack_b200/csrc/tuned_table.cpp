@@ -250,6 +250,10 @@ bool parse_kernel_name(const std::string& name, int* tm, int* bn, int* sp) {
 
 int tuned_validate(int M, int N, int K, int tile_m, int tile_n, int split_k) {
   if (M < 1 || N < 128 || K < 128 || N % 128 || K % 128 || M > 65535 * 128) return FACK_ERR_BAD_SHAPE;
+  if (tile_n == 16) {  // warp-MMA small-M kernel: 16 weight rows, up to 16 tokens, no K split
+    if (tile_m != 16 || M > tile_m || split_k != 1 || K / 128 > 256) return FACK_ERR_BAD_ARG;
+    return FACK_OK;
+  }
   if (tile_m == 16 || tile_m == 32 || tile_m == 64) {  // swapped small-M tiles: 128 weight rows, all M tokens
     if (M > tile_m || tile_n != 128 || split_k < 1 || split_k > kTunedMaxSplit || split_k > K / 128 ||
         (K / 128 + split_k - 1) / split_k > 128)

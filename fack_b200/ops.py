@@ -91,8 +91,11 @@ def parse_kernel_name(name) -> tuple:
     applies here, so they (and None / "") leave the choice to the library."""
     if not name or name in AITER_SYMBOLS:
         return 0, 0, 0
-    m = re.fullmatch(KERNEL_PREFIX + r"_t(16|32|64|128|256)x(64|128|224|256)_s([1-8])", str(name))
-    if not m or (m.group(1) == "256" and int(m.group(3)) > 4) or (int(m.group(1)) < 128 and m.group(2) != "128") \
+    m = re.fullmatch(KERNEL_PREFIX + r"_t(16|32|64|128|256)x(16|64|128|224|256)_s([1-8])", str(name))
+    small = m is not None and m.group(2) == "16"       # the warp-MMA small-M kernel: 16 tokens, no split
+    if not m or (small and (m.group(1) != "16" or m.group(3) != "1")) \
+            or (m.group(1) == "256" and int(m.group(3)) > 4) \
+            or (not small and int(m.group(1)) < 128 and m.group(2) != "128") \
             or (m.group(2) == "224" and (m.group(1) != "128" or m.group(3) != "1")):
         raise ValueError(f"unknown blockscale kernel {name!r}")
     return int(m.group(1)), int(m.group(2)), int(m.group(3))

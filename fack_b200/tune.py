@@ -6,8 +6,9 @@
 For every (M, N, K) the tuner times each valid plan of the kernel --
 token tile 128 (one CTA) or 256 (a CTA pair), weight tile 64, 128 or 256
 dividing N, split-K 1..min(8, K/128) (pairs: 1..4), the 224-wide weight tile
-(one K slice) when 224 divides N, and for M <= 64 the swapped
-16/32/64-token tiles -- through the same entry
+(one K slice) when 224 divides N, for M <= 64 the swapped
+16/32/64-token tiles, and for M <= 16 the warp-MMA kernel's 16-row weight
+tiles -- through the same entry
 the reference calls (pre-packed weight, transposed x_scale, split-K slices
 combined in distributed shared memory), checks each plan's output against an
 fp32 dequantise-then-matmul on the device, and writes the fastest plan per
@@ -105,6 +106,8 @@ def candidates(M: int, N: int, K: int) -> list:
                 plans.append((tm, tn, sk))
     if N % 224 == 0:                             # 224-wide tiles: persistent kernel, one K slice
         plans.append((128, 224, 1))
+    if M <= 16 and KB <= 256:                    # the warp-MMA small-M kernel: 16-row weight tiles
+        plans.append((16, 16, 1))
     return plans
 
 

@@ -93,8 +93,12 @@ const char* fack_last_error(void);
  * library's choice; a 224-wide weight tile (four per 896 columns: one rank's
  * shard of a 7168-wide layer over 8 GPUs) is valid with 128-token tiles and
  * one K slice only, runs on the persistent kernel, and is chosen by request
- * or by a tuned-table row, never by the cost model -- and the workspace bytes fack_gemm_bs_ex needs for that
- * plan when the caller supplies a workspace (0 for a single K slice).  A
+ * or by a tuned-table row, never by the cost model; a 16-wide weight tile
+ * (tile_m 16 or 0, split-K 1 or 0, M <= 16, K <= 256 x 128) is the small-M
+ * kernel -- 16 weight rows per CTA, K split among the CTA's warps, no
+ * workspace -- which the cost model picks for M <= 8 -- and the workspace bytes
+ * fack_gemm_bs_ex needs for that plan when the caller supplies a workspace
+ * (0 for a single K slice).  A
  * library choice of split-K queries the current device (cluster occupancy); an
  * explicit split does not.  When all three requests are 0, an exact-shape row
  * of the tuned table (fack_gemm_bs_tuned_*) for the current device's SM count

@@ -87,6 +87,14 @@ def test_explicit_split_plan_and_workspace_without_device():
     assert plan(8192, 896, 16384, n=224, s=2)[0] == _lib.FACK_ERR_BAD_ARG
     assert plan(8192, 896, 16384, m=256, n=224)[0] == _lib.FACK_ERR_BAD_ARG
     assert plan(8192, 1024, 16384, n=224)[0] == _lib.FACK_ERR_BAD_ARG
+    # the warp-MMA small-M kernel (16-row weight tiles): up to 16 tokens, one slice, K <= 256 blocks
+    assert plan(1, 3072, 7168, n=16) == (0, 16, 16, 1, 0)
+    assert plan(16, 3072, 7168, m=16, n=16, s=1) == (0, 16, 16, 1, 0)
+    assert plan(17, 3072, 7168, n=16)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8, 3072, 7168, m=32, n=16)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8, 3072, 7168, n=16, s=2)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8, 3072, 257 * 128, n=16)[0] == _lib.FACK_ERR_BAD_ARG
+    assert plan(8, 3072, 7168, m=16, s=1)[2] == 128          # a 16-token tile alone is the swapped kernel
     tn2, sk2 = ctypes.c_int(), ctypes.c_int()
     assert lib.fack_gemm_bs_select(256, 3072, 7168, 6, ctypes.byref(tn2), ctypes.byref(sk2)) == 0
     assert (tn2.value, sk2.value) == (256, 6)

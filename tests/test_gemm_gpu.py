@@ -72,6 +72,11 @@ def test_golden_every_tile_and_split(cuda_device, name, packed):
                                                         kernelName=f"fack_bs_sm100_t{tile_m}x{tile}_s{split}",
                                                         bpreshuffle=packed)
                 assert_close(out, g["reference"], f"{name} tile={tile_m}x{tile} split={split} packed={packed}")
+    if g["m"] <= 16 and g["k"] // 128 <= 256:          # the warp-MMA small-M kernel
+        out = poisoned(g["m"], g["n"], cuda_device)
+        fb.gemm_a8w8_blockscale_bpreshuffle_asm(g["a"], b, out, g["packed_sa"], g["sb"], splitK=1,
+                                                kernelName="fack_bs_sm100_t16x16_s1", bpreshuffle=packed)
+        assert_close(out, g["reference"], f"{name} tile=16x16 packed={packed}")
 
 
 @pytest.mark.parametrize("name", golden_names())
@@ -157,6 +162,59 @@ def test_small_m_swapped_tiles_vs_oracle(cuda_device, decode_weights, m):
     for _ in range(3):
         again = fb.gemm_blockscale(xq_d, packed, xs.to(d), ws_d, split_k=6, tile_m=32 if m <= 32 else 64)
         assert torch.equal(again.view(torch.int16), first.view(torch.int16))
+
+
+@pytest.mark.parametrize("m", [1, 2, 5, 8, 9, 15, 16])
+def test_small_m_warp_mma_kernel_vs_oracle(cuda_device, decode_weights, m):
+    """The warp-MMA small-M kernel (16-row weight tiles, fack_bs_sm100_t16x16_s1)
+    at N=3072, K=7168: packed and row-major weights, the aiter x_scale form and
+    the native one, bitwise repeatable; the cost model's own plan for M <= 8."""
+    wq, ws = decode_weights
+    xq, xs = data.make_activations(m, 7168, "normal", seed=500 + m)
+    ref = orc.reference_gemm(xq, wq, xs, ws)
+    d = cuda_device
+    packed = fb.shuffle_weight(wq.to(d))
+    xq_d, ws_d = xq.to(d), ws.to(d)
+    name = "fack_bs_sm100_t16x16_s1"
+    out = poisoned(m, 3072, d)
+    fb.gemm_a8w8_blockscale_bpreshuffle_asm(xq_d, packed, out, data.to_aiter_xscale(xs).to(d), ws_d, splitK=1,
+                                            kernelName=name)
+    assert_close(out, ref, f"M={m} packed, aiter x_scale")
+    y_row = fb.gemm_blockscale(xq_d, wq.to(d), xs.to(d), ws_d, tile_m=16, tile_n=16)
+    assert_close(y_row, ref, f"M={m} row-major")
+    assert torch.equal(y_row.view(torch.int16), out.view(torch.int16))   # same arithmetic, same bits
+    for _ in range(3):
+        again = fb.gemm_blockscale(xq_d, packed, xs.to(d), ws_d, tile_m=16, tile_n=16)
+        assert torch.equal(again.view(torch.int16), out.view(torch.int16))
+    from fack_b200 import _lib
+    lib = _lib.load()
+    lib.fack_gemm_bs_tuned_clear()
+    try:
+        assert (fb.get_config(m, 3072, 7168)["kernelName"] == name) == (m <= 8)
+    finally:
+        for table in _lib.tuned_tables():
+            _lib.load_tuned(table, lib)
+
+
+@pytest.mark.parametrize("shape", [(3, 128, 128), (16, 256, 896), (7, 1024, 256 * 128), (11, 4096, 2048)])
+def test_small_m_warp_mma_kernel_edges(cuda_device, shape):
+    """Edges of the small-M kernel: one K block (seven of eight warps idle),
+    the largest K it takes (256 blocks), a single 128-row weight block, and
+    strided operands (ldx > K, Y inside a wider tensor)."""
+    M, N, K = shape
+    d = cuda_device
+    xq, xs, wq, ws = data.make_inputs(data.Workload("t", M, N, K), seed=M + N)
+    ref = orc.reference_gemm(xq, wq, xs, ws) if K <= 4096 else None
+    xbig = torch.zeros((M, K + 256), dtype=torch.float8_e4m3fn, device=d)
+    xbig[:, 128:128 + K] = xq.to(d)
+    big = torch.full((M, N + 512), float("nan"), dtype=torch.bfloat16, device=d)
+    view = big[:, 256:256 + N]
+    fb.gemm_blockscale(xbig[:, 128:128 + K], fb.shuffle_weight(wq.to(d)), xs.to(d), ws.to(d), out=view,
+                       tile_m=16, tile_n=16)
+    assert torch.isnan(big[:, :256].float()).all() and torch.isnan(big[:, 256 + N:].float()).all()
+    if ref is None:   # the long-K case: against the library's swapped kernel (itself checked against the oracle)
+        ref = fb.gemm_blockscale(xq.to(d), wq.to(d), xs.to(d), ws.to(d), tile_m=16, split_k=8)
+    assert_close(view, ref, f"{shape}")
 
 
 def test_plumbing_shape_vs_oracle(cuda_device):

@@ -152,3 +152,14 @@ def test_kernel_names_with_224_wide_tiles():
     for bad in ("fack_bs_sm100_t128x224_s2", "fack_bs_sm100_t256x224_s1", "fack_bs_sm100_t64x224_s1"):
         with pytest.raises(ValueError):
             ops.parse_kernel_name(bad)
+
+
+def test_kernel_names_of_the_small_m_kernel():
+    """fack_bs_sm100_t16x16_s1 names the warp-MMA small-M kernel; it has no
+    other token tile and no split."""
+    from fack_b200 import ops
+    assert ops.parse_kernel_name("fack_bs_sm100_t16x16_s1") == (16, 16, 1)
+    assert ops.kernel_name(16, 16, 1) == "fack_bs_sm100_t16x16_s1"
+    for bad in ("fack_bs_sm100_t32x16_s1", "fack_bs_sm100_t16x16_s2", "fack_bs_sm100_t128x16_s1"):
+        with pytest.raises(ValueError):
+            ops.parse_kernel_name(bad)

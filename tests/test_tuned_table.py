@@ -59,6 +59,10 @@ def test_set_lookup_replace_clear(lib):
     ((148, 8192, 896, 16384, 128, 224, 2), _lib.FACK_ERR_BAD_ARG),  # 224-wide tiles: one K slice only
     ((148, 8192, 896, 16384, 256, 224, 1), _lib.FACK_ERR_BAD_ARG),  # 224-wide tiles: single CTAs only
     ((148, 8192, 1024, 16384, 128, 224, 1), _lib.FACK_ERR_BAD_ARG),  # 224 does not divide 1024
+    ((148, 17, 3072, 7168, 16, 16, 1), _lib.FACK_ERR_BAD_ARG),      # small-M kernel: at most 16 tokens
+    ((148, 8, 3072, 7168, 32, 16, 1), _lib.FACK_ERR_BAD_ARG),       # small-M kernel: 16-token tile only
+    ((148, 8, 3072, 7168, 16, 16, 2), _lib.FACK_ERR_BAD_ARG),       # small-M kernel: no split
+    ((148, 8, 3072, 257 * 128, 16, 16, 1), _lib.FACK_ERR_BAD_ARG),  # small-M kernel: K <= 256 blocks
 ])
 def test_invalid_rows_refused(lib, row, status):
     assert lib.fack_gemm_bs_tuned_set(*row) == status
@@ -146,7 +150,7 @@ def test_tuner_candidates_are_exactly_the_valid_plans():
                                          ctypes.byref(nb)) == 0
             assert (tm.value, tn.value, sk.value) == c
         for t_m in (16, 32, 64, 128, 256):
-            for t_n in (64, 128, 224, 256):
+            for t_n in (16, 64, 128, 224, 256):
                 for s in range(1, 9):
                     ok = lib.fack_gemm_bs_plan(M, N, K, t_m, t_n, s, ctypes.byref(tm), ctypes.byref(tn),
                                                ctypes.byref(sk), ctypes.byref(nb)) == 0
