@@ -33,6 +33,7 @@ RTOL = ATOL = 1e-2
 # (name, M, N, K, x distribution, w distribution, rows sampled for the oracle)
 CASES = [
     ("small_wide", 32, 8192, 1024, "uniform", "uniform_logscale", 32),
+    ("tiny_m", 5, 4096, 2048, "normal", "normal", 5),          # the warp-MMA small-M kernel with peers
     ("small_ragged", 300, 2048, 768, "outlier", "normal", 300),
     ("prefill", 8192, 7168, 16384, "outlier", "normal", 24),
     ("wide_constant", 32, 65536, 7168, "constant", "uniform_logscale", 32),
