@@ -2097,17 +2097,18 @@ static int plan_auto(DeviceInfo* d, int M, int N, int K, int tm_req, int bn_req,
   // swapped small-M tiles: the requested one, else the smallest token tile
   // that holds all M tokens
   const int tm_swap = tm_req && tm_req < kTileM ? tm_req : tm_req ? 0 : M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
-  // the warp-MMA small-M kernel for up to 8 tokens (only when no tile is
-  // requested: a requested 16-token tile alone means the swapped kernel).
-  // Paired A/B at N=3072, K=7168 against the swapped kernel's 16 x 128 split-5
-  // plan: 1.07-1.10x at M=1, 1.07x at M=8, even at M=4, 0.93x at M=16 (its
-  // second token group doubles the MMAs and the token bytes per K block).
-  if (!tm_req && !bn_req && M <= 8 && KB <= kSmallMaxKb) {
-    const int tm_small = 16;
-    best = plan_cost(d, M, N, K, tm_small, kSmallRows, 1);
-    bt = tm_small;
-    bb = kSmallRows;
-    bs = 1;
+  // The warp-MMA small-M kernel, when no tile is requested (a requested
+  // 16-token tile alone means the swapped kernel).  Paired A/B at K = 7168
+  // on B200: faster than the swapped
+  // 16 x 128 tiles at M <= 8 for every N (1.07-1.10x at N = 3072) and at
+  // M <= 16 for N >= 8192 (1.10-1.12x), and than the 128 x 256 tiles by
+  // 1.13-1.51x at N = 8192-16384 (even at 65536); the swapped kernel keeps
+  // 9 <= M <= 16 at N <= 4096 (16 x 3072: 8.5 against 9.1 us).
+  if (!tm_req && !bn_req && M <= 16 && KB <= kSmallMaxKb && (M <= 8 || N > 4096)) {
+    *tm_out = 16;
+    *bn_out = kSmallRows;
+    *sp_out = 1;
+    return FACK_OK;
   }
   if (tm_swap && M <= tm_swap && (bn_req == 0 || bn_req == kBlk)) {
     for (int sp = 1; sp <= KB && sp <= kMaxSplit; ++sp) {
