@@ -96,7 +96,8 @@ const char* fack_last_error(void);
  * or by a tuned-table row, never by the cost model; a 16-wide weight tile
  * (tile_m 16 or 0, split-K 1 or 0, M <= 16, K <= 256 x 128) is the small-M
  * kernel -- 16 weight rows per CTA, K split among the CTA's warps, no
- * workspace -- which the cost model picks for M <= 8 -- and the workspace bytes
+ * workspace -- which the library picks for M <= 8, and for M <= 16 when
+ * N > 4096 -- and the workspace bytes
  * fack_gemm_bs_ex needs for that plan when the caller supplies a workspace
  * (0 for a single K slice).  A
  * library choice of split-K queries the current device (cluster occupancy); an
