@@ -196,6 +196,27 @@ def test_small_m_warp_mma_kernel_vs_oracle(cuda_device, decode_weights, m):
             _lib.load_tuned(table, lib)
 
 
+def test_small_m_planner_choice(cuda_device):
+    """Without table rows: the warp-MMA kernel for M <= 8 at any N and for
+    M <= 16 above N = 4096, the swapped kernel for 9 <= M <= 16 at N <= 4096,
+    neither from M = 17; a K beyond the kernel's scale table leaves it out."""
+    from fack_b200 import _lib
+    lib = _lib.load()
+    lib.fack_gemm_bs_tuned_clear()
+    try:
+        name = lambda m, n, k: fb.get_config(m, n, k)["kernelName"]   # noqa: E731
+        small = "fack_bs_sm100_t16x16_s1"
+        for m, n in ((1, 3072), (4, 3072), (8, 65536), (9, 8192), (12, 8192), (16, 65536)):
+            assert name(m, n, 7168) == small, (m, n)
+        assert name(12, 3072, 7168).startswith("fack_bs_sm100_t16x128_")
+        assert name(16, 4096, 7168).startswith("fack_bs_sm100_t16x128_")
+        assert name(17, 8192, 7168) != small
+        assert name(4, 3072, 257 * 128) != small
+    finally:
+        for table in _lib.tuned_tables():
+            _lib.load_tuned(table, lib)
+
+
 @pytest.mark.parametrize("shape", [(3, 128, 128), (16, 256, 896), (7, 1024, 256 * 128), (11, 4096, 2048)])
 def test_small_m_warp_mma_kernel_edges(cuda_device, shape):
     """Edges of the small-M kernel: one K block (seven of eight warps idle),
