@@ -101,8 +101,9 @@ def test_shard_bounds_and_weight_slices():
 # ys[j]; the fake IPC layer hands out addresses (j + 1) << 40 + byte offset, and
 # the fake GEMM resolves them, so the test checks the handle exchange, the
 # offset arithmetic and when the real ShardedBlockscaleGemm adds an exchange
-# step of its own.  On the GPU the launch's last CTA signals the peers and
-# waits for theirs; here a gloo barrier after the stores stands in for it.
+# step of its own.  On the GPU each CTA of the launch counts its landed stores
+# into the peers' exchange states and CTA 0 waits for the peers' counts; here a
+# gloo barrier after the stores stands in for it.
 
 class _FakeIpc:
     """Handles name (rank, buffer id); rank j's buffer b maps to
